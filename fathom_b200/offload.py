@@ -1,0 +1,175 @@
+"""Host-resident regime: bit-plane index and bf16 K/V rows in pinned, mapped host memory.
+
+Mirrors the pieces of `scripts/B_e2e_offload_v2.py` that sit on the decode step:
+  host_mapped / free_host / DevPtr   :29-39   (here through fathom_host_alloc_mapped)
+  build_store (copy-index order)     :41-60, 267, 299-309
+  gather_rows                        :73-83
+  offload_attn (planes method)       :163-244 (plan, scan, sink/local top-k, unique-row gather,
+                                               exact attention)
+The scan reads the host store directly over the host link (zero-copy loads, one contiguous
+run per (kv-head, channel, plane) in the SUB = nblk order); the rows are gathered once per
+unique index per KV head.  Everything runs on CUDA kernels of libfathom_b200.so.
+"""
+import ctypes
+import math
+
+import torch
+
+from . import _lib, bitplane as bp
+from ._lib import check, lib, ptr, require_cuda, stream_of
+
+_CAI_TYPESTR = {torch.int8: "|i1", torch.uint8: "|u1", torch.int16: "<i2", torch.int32: "<i4", torch.int64: "<i8",
+                torch.float16: "<f2", torch.float32: "<f4"}
+
+
+class DevPtr:
+    """Device address with a dtype (scripts/B_e2e_offload_v2.py:30-32)."""
+
+    def __init__(self, ptr_, dtype):
+        self.ptr, self.dtype = ptr_, dtype
+
+    def data_ptr(self):
+        return self.ptr
+
+
+class _CudaArray:
+    def __init__(self, dev_ptr, shape, typestr):
+        self.__cuda_array_interface__ = {"shape": tuple(shape), "typestr": typestr, "data": (dev_ptr, False),
+                                         "version": 3, "strides": None}
+
+
+class MappedBuffer:
+    """Pinned, portable, mapped host allocation of `shape`/`dtype`.
+
+    .host  CPU tensor view of the memory (for filling / checking on the host)
+    .dev   CUDA tensor aliasing the same memory through its device address: kernels that read it
+           pull the bytes over the host link (zero-copy)
+    Freed with .free() or when garbage-collected."""
+
+    def __init__(self, shape, dtype, device=None):
+        self.shape, self.dtype = tuple(shape), dtype
+        elem = torch.empty((), dtype=dtype).element_size()
+        self.nbytes = int(math.prod(self.shape)) * elem
+        hp, dp = ctypes.c_void_p(), ctypes.c_void_p()
+        check(lib().fathom_host_alloc_mapped(self.nbytes, ctypes.byref(hp), ctypes.byref(dp)), "host_alloc_mapped")
+        self.hp, self.dp = hp.value, dp.value
+        raw = (ctypes.c_byte * self.nbytes).from_address(self.hp)
+        self.host = torch.frombuffer(raw, dtype=dtype).view(self.shape)
+        cai_dtype = torch.int16 if dtype == torch.bfloat16 else dtype
+        device = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+        alias = torch.as_tensor(_CudaArray(self.dp, self.shape, _CAI_TYPESTR[cai_dtype]), device=device)
+        self.dev = alias.view(dtype) if cai_dtype != dtype else alias
+
+    def free(self):
+        if getattr(self, "hp", None):
+            self.host = self.dev = None
+            lib().fathom_host_free(self.hp)
+            self.hp = None
+
+    def __del__(self):
+        try:
+            self.free()
+        except Exception:
+            pass
+
+
+_live = {}
+
+
+def host_mapped(t):
+    """Copy tensor t into pinned, GPU-mapped host memory (scripts/B_e2e_offload_v2.py:33-38).
+    Returns (cpu view tensor, DevPtr for kernels, host pointer)."""
+    buf = MappedBuffer(t.shape, t.dtype, t.device if t.is_cuda else None)
+    if t.is_cuda:
+        buf.dev.copy_(t)
+    else:
+        buf.host.copy_(t)
+    _live[buf.hp] = buf
+    return buf.host, DevPtr(buf.dp, t.dtype), buf.hp
+
+
+def free_host(hp):
+    """scripts/B_e2e_offload_v2.py:39."""
+    buf = _live.pop(hp, None)
+    if buf is not None:
+        buf.free()
+
+
+class HostPlaneStore(bp.PlaneStore):
+    """A PlaneStore whose planes and scales live in pinned, mapped host memory in the copy-index order
+    (SUB = nblk: every (bh, channel, plane) is one contiguous run of nblk*8 bytes).
+
+    Built on the GPU by the fused quantise+pack kernel, then copied to the host; the device copy is
+    released.  scan() reads the host memory directly (zero-copy), with the same kernel as the HBM
+    store."""
+
+    def __init__(self, K, scale_dtype=torch.float16):
+        require_cuda(K)
+        old = bp.SUB
+        try:
+            bp.SUB = math.ceil(K.shape[1] / bp.BLK)
+            super().__init__(K, scale_dtype)
+        finally:
+            bp.SUB = old
+        self.planes_buf = MappedBuffer(self.planes_k.shape, torch.int64, K.device)
+        self.scales_buf = MappedBuffer(self.scales_k.shape, torch.float16, K.device)
+        self.planes_buf.dev.copy_(self.planes_k)
+        self.scales_buf.dev.copy_(self.scales_k)
+        torch.cuda.current_stream(K.device).synchronize()
+        self.planes_k = self.planes_buf.dev
+        self.planes32 = self.planes_k.view(torch.int32)
+        self.scales_k = self.scales_buf.dev
+
+    def free(self):
+        self.planes_k = self.planes32 = self.scales_k = None
+        self.planes_buf.free()
+        self.scales_buf.free()
+
+
+def gather_rows(src, cap, idx, BH, dtype=torch.bfloat16, D=128):
+    """dst[bh, r, :] = src[bh, idx[bh, r], :] for bf16 rows; idx < 0 leaves the row zero; src may be a
+    mapped host alias (scripts/B_e2e_offload_v2.py:73-83)."""
+    require_cuda(idx)
+    idx = idx.to(torch.int32).contiguous()
+    R = idx.shape[1]
+    dst = torch.zeros(BH, R, D, device=idx.device, dtype=dtype)
+    check(lib().fathom_gather_rows(ptr(src), cap, ptr(idx), BH, R, D, ptr(dst), stream_of(idx.device)),
+          "gather_rows")
+    return dst
+
+
+def decode_attention(q, idx, K_src, V_src, cap, n_host=None, K_recent=None, V_recent=None, recent_cap=0,
+                     out_dtype=torch.float32):
+    """Exact attention over the selected rows (scripts/B_e2e_offload_v2.py:226-244):
+    q [BH, G, 128] fp32, idx [BH, G, k] int64.  Unique indices of a KV head are fetched once; an index
+    >= n_host reads row idx - n_host of the device-resident recent buffers [BH, recent_cap, 128].
+    Returns [BH, G, 128] in out_dtype (float32 or bfloat16)."""
+    require_cuda(q, idx)
+    BH, G, D = q.shape
+    k = idx.shape[-1]
+    n_host = cap if n_host is None else n_host
+    dev = q.device
+    qc = q.contiguous().float()
+    ic = idx.contiguous().to(torch.int64)
+    out = torch.empty(BH, G, D, device=dev, dtype=out_dtype)
+    if out_dtype not in (torch.float32, torch.bfloat16):
+        raise TypeError("decode_attention: out_dtype must be float32 or bfloat16")
+    ws = _lib.workspace(dev, lib().fathom_decode_workspace_bytes(BH, G, k), "decode")
+    check(lib().fathom_decode_attention(ptr(qc), BH, G, ptr(ic), k, ptr(K_src), ptr(V_src), cap, n_host,
+                                        ptr(K_recent), ptr(V_recent), recent_cap,
+                                        ptr(out) if out_dtype == torch.float32 else None,
+                                        ptr(out) if out_dtype == torch.bfloat16 else None,
+                                        ptr(ws), ws.numel(), stream_of(dev)), "decode_attention")
+    return out
+
+
+def decode_step(q, g, budget, store, K_src, V_src, cap, k=580, sink=4, local=64, n_host=None, K_recent=None,
+                V_recent=None, recent_cap=0, scores=None, out_dtype=torch.float32):
+    """One layer of an offloaded decode step (offload_attn, scripts/B_e2e_offload_v2.py:180-244, planes
+    method): plan -> plane-prefix scan of the (host or HBM) store -> sink+local top-k -> unique-row
+    gather + exact attention.  Returns (out [BH,G,128], idx [BH,G,k])."""
+    plan = bp.make_plan(g, budget)
+    s = store.scan(q, plan, out=scores)
+    idx = bp.sink_local_topk(s, k, sink, local)
+    out = decode_attention(q, idx, K_src, V_src, cap, n_host, K_recent, V_recent, recent_cap, out_dtype)
+    return out, idx

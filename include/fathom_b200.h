@@ -1,0 +1,166 @@
+/*
+ * fathom_b200 -- C ABI of the B200 (sm_100a) key-scan library.
+ *
+ * Every entry point takes plain device pointers (or device aliases of pinned,
+ * mapped host memory), sizes, and a CUDA stream passed as `void*`
+ * (a cudaStream_t; NULL = the legacy default stream).  Work is enqueued on that
+ * stream and the call returns without synchronising.  Every function returns
+ * FATHOM_OK (0) or a negative status; fathom_last_error() then holds a message
+ * for the calling thread.  No function allocates device memory except
+ * fathom_host_alloc_mapped; scratch space is a caller-provided workspace whose
+ * size the matching *_workspace_bytes() function returns.
+ *
+ * Store layout ("superblock order", reference kernels/bitplane.py:7-11, 60-65):
+ *   planes_k [BH][nsb][128][4][sub]  uint64   bit i of word (bh,sb,j,p,s) is bit p
+ *                                             (p = 0 = MSB) of the 4-bit code of token
+ *                                             64*(sb*sub+s)+i, channel j
+ *   scales_k [BH][nsb][128][sub]     fp16     absmax of block sb*sub+s, channel j
+ *   nsb = ceil(nblk / sub), nblk = ceil(n / 64); pad blocks hold zero words/scales.
+ * sub = 16 is the HBM order; sub = nblk is the host "copy-index" order in which
+ * every (bh, channel, plane) is one contiguous run (scripts/B_e2e_offload_v2.py:267);
+ * sub = 1 is the logical order of pack_planes (kernels/bitplane.py:44-50).
+ */
+#ifndef FATHOM_B200_H
+#define FATHOM_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum {
+  FATHOM_OK = 0,
+  FATHOM_ERR_NULL = -1,        /* a required pointer is NULL */
+  FATHOM_ERR_SHAPE = -2,       /* a size / shape / range argument is invalid */
+  FATHOM_ERR_UNSUPPORTED = -3, /* valid request outside what this build implements */
+  FATHOM_ERR_CUDA = -4,        /* a CUDA runtime call or a kernel launch failed */
+  FATHOM_ERR_WORKSPACE = -5    /* caller workspace too small or misaligned */
+};
+
+enum { FATHOM_DTYPE_F32 = 0, FATHOM_DTYPE_BF16 = 1, FATHOM_DTYPE_F16 = 2 };
+
+/* Message of the last failing call on this thread ("" if none). */
+const char* fathom_last_error(void);
+/* ABI version of this library (bumped on any signature change). */
+int fathom_abi_version(void);
+
+/* ---------------------------------------------------------------- store build */
+
+/* Quantise keys to 4-bit codes and pack them into bit planes in one pass.
+ * Replaces quantise_u4 + pack_planes + to_superblocks (kernels/bitplane.py:23-32,
+ * 44-50, 60-65) as used by PlaneStore.__init__ (kernels/bitplane.py:312-316).
+ *   K          [BH][n][128] rows of k_dtype; row bh starts at K + bh*k_stride_bh elements
+ *   amax_f16   1: the block absmax is rounded to fp16 before the codes are computed
+ *              (scale_dtype=float16, the default); 0: fp32 absmax (scale_dtype=float32)
+ * Outputs (each may be NULL):
+ *   code       [BH][n][128] uint8 codes in [0, 16)
+ *   scales_blk [BH][nblk][128] absmax, fp32 if scales_blk_f32 else fp16
+ *   planes_k / scales_k   the store in superblock order `sub` (see above); pad
+ *              blocks up to nsb*sub are written with zeros. */
+int fathom_quantise_pack(const void* K, int k_dtype, int64_t BH, int64_t n, int64_t k_stride_bh,
+                         int64_t sub, int amax_f16, uint8_t* code, void* scales_blk, int scales_blk_f32,
+                         uint64_t* planes_k, uint16_t* scales_k, void* stream);
+
+/* Codes [BH][n][128] uint8 -> planes in superblock order `sub` (sub = 1: pack_planes,
+ * kernels/bitplane.py:44-50).  Pad tokens and pad blocks are zero. */
+int fathom_pack_codes(const uint8_t* code, int64_t BH, int64_t n, int64_t sub, uint64_t* planes_k, void* stream);
+
+/* Planes in superblock order `sub` -> codes [BH][n][128] uint8 (unpack_planes,
+ * kernels/bitplane.py:52-58, with sub = 1). */
+int fathom_unpack_planes(const uint64_t* planes_k, int64_t BH, int64_t n, int64_t sub, uint8_t* code, void* stream);
+
+/* Re-order a store between superblock orders (to_superblocks, kernels/bitplane.py:60-65,
+ * is sub_src = 1 -> sub_dst = SUB).  Either pair of pointers may be NULL. */
+int fathom_relayout(const uint64_t* planes_src, const uint16_t* scales_src, int64_t BH, int64_t nblk, int64_t sub_src,
+                    uint64_t* planes_dst, uint16_t* scales_dst, int64_t sub_dst, void* stream);
+
+/* ---------------------------------------------------------------- plan */
+
+/* Per-(batch, kv-head) reverse water-filling plan (plan_kernel + make_plan,
+ * kernels/bitplane.py:83-116; depths equal make_plan_torch, :118-126).
+ *   g [BH][128] fp32 gains; budget [BH] fp32 bits per token.
+ *   t [BH][128] int8; pairs [BH][128*bmax], npairs [BH]; act [BH][128], nact [BH];
+ *   cls [BH][bmax][128], clsn [BH][bmax] (int32).  List tails are zero-filled.
+ *   bmax in 1..4; iters >= 0. */
+int fathom_make_plan(const float* g, const float* budget, int64_t BH, int bmax, int iters, int8_t* t, int32_t* pairs,
+                     int32_t* npairs, int32_t* act, int32_t* nact, int32_t* cls, int32_t* clsn, void* stream);
+
+/* ---------------------------------------------------------------- scan */
+
+/* Plane-prefix scan (PlaneStore.scan -> scan_planes_cls_kernel, kernels/bitplane.py:319-338,
+ * 275-307): scores[bh][g][tok] = sum_j q[bh][g][j] * value_{t_j}(tok, j) over the channels
+ * of the depth-class lists, reading only the first t_j planes of channel j.
+ *   q [BH][G][128] fp32, G in 1..8; cls/clsn from fathom_make_plan (stride bmax);
+ *   planes_k/scales_k in order `sub`, device memory or a mapped host alias;
+ *   tokens of blocks [blk_begin, blk_end) are written to scores [BH][G][n]; others untouched. */
+int fathom_scan(const float* q, int64_t BH, int G, int64_t n, int64_t sub, const int32_t* cls, const int32_t* clsn,
+                int bmax, const uint64_t* planes_k, const uint16_t* scales_k, int64_t blk_begin, int64_t blk_end,
+                float* scores, void* stream);
+
+/* ---------------------------------------------------------------- selection */
+
+/* Workspace bytes fathom_select_topk / fathom_sink_local_topk need for `rows` rows. */
+size_t fathom_select_workspace_bytes(int64_t rows, int64_t n, int64_t kk);
+
+/* Top-kk of each row of scores [rows][n] (row r at scores + r*row_stride), with tokens
+ * outside [mask_lo, mask_hi) treated as -inf.  Output indices (plus index_offset) in the
+ * order (score descending, index ascending) to out_idx [rows][out_stride] int64, and the
+ * selected scores to out_scores [rows][kk] if not NULL.  kk in 1..4096, kk <= n.
+ * The selection step of sink_local_topk (kernels/bitplane.py:372-378, torch.topk :376). */
+int fathom_select_topk(const float* scores, int64_t rows, int64_t n, int64_t row_stride, int64_t kk, int64_t mask_lo,
+                       int64_t mask_hi, int64_t index_offset, int64_t* out_idx, int64_t out_stride, float* out_scores,
+                       void* workspace, size_t workspace_bytes, void* stream);
+
+/* sink_local_topk (kernels/bitplane.py:372-378): idx [rows][k] int64 = the top (k-sink-local)
+ * of tokens [sink, n-local) followed by 0..sink-1 and n-local..n-1. */
+int fathom_sink_local_topk(const float* scores, int64_t rows, int64_t n, int64_t k, int64_t sink, int64_t local,
+                           int64_t* idx, void* workspace, size_t workspace_bytes, void* stream);
+
+/* Final top-kk of candidate lists [rows][m] (scores, global int64 indices < 2^32) in the
+ * (score descending, index ascending) order: the merge of per-shard candidates of a
+ * context-sharded scan.  No reference counterpart (the reference runs on one GPU);
+ * it restates the top-k of sink_local_topk (kernels/bitplane.py:376) over a union.
+ * m in 1..8192, kk <= m. */
+int fathom_merge_topk(const float* cand_scores, const int64_t* cand_idx, int64_t rows, int64_t m, int64_t kk,
+                      int64_t* out_idx, float* out_scores, void* stream);
+
+/* ---------------------------------------------------------------- rows + attention */
+
+/* dst[bh][r][:] = src[bh][idx[bh][r]][:] for bf16 rows of D (D*2 a multiple of 16);
+ * idx < 0 skips the row (no traffic, dst row untouched).  src may be a mapped host alias
+ * (gather_rows_kernel, scripts/B_e2e_offload_v2.py:73-83). */
+int fathom_gather_rows(const uint16_t* src, int64_t cap, const int32_t* idx, int64_t BH, int64_t R, int64_t D,
+                       uint16_t* dst, void* stream);
+
+/* Workspace bytes of fathom_decode_attention. */
+size_t fathom_decode_workspace_bytes(int64_t BH, int G, int64_t k);
+
+/* Decode attention over selected rows (offload_attn tail, scripts/B_e2e_offload_v2.py:226-244;
+ * HBM twin gather_attn, scripts/B_kernel_bench.py:26-31):
+ *   q [BH][G][128] fp32; idx [BH][G][k] int64 token indices.
+ *   Each unique index of a KV head is fetched once.  Index < n_host reads row idx of
+ *   K_src/V_src [BH][cap][128] bf16 (device memory or mapped host alias); index >= n_host
+ *   reads row idx-n_host of K_recent/V_recent [BH][recent_cap][128] bf16 (device).
+ *   out = softmax(q K_sel^T / sqrt(128)) V_sel in fp32 math, to out_f32 [BH][G][128]
+ *   and/or out_bf16 (either may be NULL). */
+int fathom_decode_attention(const float* q, int64_t BH, int G, const int64_t* idx, int64_t k, const uint16_t* K_src,
+                            const uint16_t* V_src, int64_t cap, int64_t n_host, const uint16_t* K_recent,
+                            const uint16_t* V_recent, int64_t recent_cap, float* out_f32, uint16_t* out_bf16,
+                            void* workspace, size_t workspace_bytes, void* stream);
+
+/* ---------------------------------------------------------------- host memory */
+
+/* Pinned, portable, mapped host allocation and its device alias (host_mapped,
+ * scripts/B_e2e_offload_v2.py:33-38, which calls cudaHostAlloc(flags=3) and
+ * cudaHostGetDevicePointer through ctypes). */
+int fathom_host_alloc_mapped(size_t bytes, void** host_ptr, void** dev_ptr);
+/* free_host (scripts/B_e2e_offload_v2.py:39). */
+int fathom_host_free(void* host_ptr);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* FATHOM_B200_H */

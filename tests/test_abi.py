@@ -1,0 +1,65 @@
+"""The C-ABI library: loads, exports every declared symbol, and rejects bad arguments with
+status codes before touching the GPU.  CPU only (no kernel is launched)."""
+import ctypes
+import os
+import re
+
+import pytest
+
+from fathom_b200 import _lib
+
+REPO = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+HEADER = os.path.join(REPO, "include", "fathom_b200.h")
+
+
+def declared():
+    src = open(HEADER).read()
+    src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+    return sorted(set(re.findall(r"\b(fathom_[a-z0-9_]+)\s*\(", src)))
+
+
+def test_library_loads_and_exports_every_declared_symbol():
+    L = _lib.lib()
+    names = declared()
+    assert len(names) >= 15
+    for name in names:
+        assert hasattr(L, name), name
+    assert set(names) == set(_lib.SIGNATURES), "ctypes signatures out of sync with the header"
+    assert L.fathom_abi_version() == 1
+
+
+def test_null_and_shape_errors_are_status_codes():
+    L = _lib.lib()
+    assert L.fathom_scan(None, 1, 4, 100, 16, None, None, 4, None, None, 0, 2, None, None) == _lib.FATHOM_ERR_NULL
+    assert b"NULL" in L.fathom_last_error()
+    p = ctypes.c_void_p(16)          # never dereferenced: validation fails first
+    assert L.fathom_scan(p, 1, 9, 100, 16, p, p, 4, p, p, 0, 2, p, None) == _lib.FATHOM_ERR_UNSUPPORTED
+    assert L.fathom_scan(p, 1, 4, 100, 16, p, p, 4, p, p, 0, 3, p, None) == _lib.FATHOM_ERR_SHAPE
+    assert L.fathom_make_plan(p, p, 4, 5, 30, p, p, p, p, p, p, p, None) == _lib.FATHOM_ERR_SHAPE
+    assert L.fathom_sink_local_topk(p, 1, 100, 10, 4, 6, p, p, 1 << 20, None) == _lib.FATHOM_ERR_SHAPE
+    need = L.fathom_select_workspace_bytes(4, 1000, 10)
+    assert need > 0
+    assert L.fathom_select_topk(p, 4, 1000, 1000, 10, 0, 1000, 0, p, 10, None, ctypes.c_void_p(256), need - 1,
+                                None) == _lib.FATHOM_ERR_WORKSPACE
+    assert L.fathom_merge_topk(p, p, 1, 9000, 10, p, None, None) == _lib.FATHOM_ERR_SHAPE
+    assert L.fathom_decode_attention(p, 2, 4, p, 20000, p, p, 10, 10, None, None, 0, p, None, p, 1 << 30,
+                                     None) == _lib.FATHOM_ERR_UNSUPPORTED
+    assert L.fathom_quantise_pack(p, 7, 1, 64, 64 * 128, 16, 1, None, None, 0, None, None, None) == \
+        _lib.FATHOM_ERR_UNSUPPORTED
+
+
+def test_python_layer_rejects_cpu_tensors():
+    import torch
+    from fathom_b200 import bitplane as bp
+    with pytest.raises(ValueError, match="CUDA"):
+        bp.quantise_u4(torch.zeros(2, 64, 128))
+    with pytest.raises(ValueError, match="CUDA"):
+        bp.make_plan(torch.zeros(2, 128), 48.0)
+    with pytest.raises(ValueError, match="CUDA"):
+        bp.sink_local_topk(torch.zeros(2, 4, 500), 100, 4, 32)
+
+
+def test_build_entry_compiles_for_sm100a():
+    from fathom_b200 import build
+    assert "arch=compute_100a,code=sm_100a" in " ".join(build.ARCH)
+    assert os.path.exists(_lib.LIB_PATH)

@@ -1,0 +1,71 @@
+"""Zero-copy row gather and decode attention against the oracle, from device memory and from pinned
+mapped host memory, with and without device-resident recent rows."""
+import numpy as np
+import pytest
+import torch
+
+from oracle import bitplane_oracle as O
+
+pytestmark = pytest.mark.gpu
+
+
+def _kv(BH, cap, seed):
+    g = torch.Generator().manual_seed(seed)
+    sc = torch.randn(BH, 1, 128, generator=g).exp()
+    K = (torch.randn(BH, cap, 128, generator=g) * sc).bfloat16()
+    V = (torch.randn(BH, cap, 128, generator=g) * sc).bfloat16()
+    return K, V
+
+
+def test_gather_rows_device_and_host():
+    from fathom_b200.offload import MappedBuffer, gather_rows
+    BH, cap, R = 3, 5000, 777
+    K, _ = _kv(BH, cap, 1)
+    idx = torch.randint(-1, cap, (BH, R), dtype=torch.int32)
+    ref = O.gather_rows(K.view(torch.int16).numpy(), idx.numpy())
+    got = gather_rows(K.cuda(), cap, idx.cuda(), BH)
+    assert np.array_equal(got.cpu().view(torch.int16).numpy(), ref)
+    hb = MappedBuffer((BH, cap, 128), torch.bfloat16)
+    hb.host.copy_(K)
+    got = gather_rows(hb.dev, cap, idx.cuda(), BH)
+    assert np.array_equal(got.cpu().view(torch.int16).numpy(), ref)
+    hb.free()
+
+
+@pytest.mark.parametrize("G,k", [(4, 580), (7, 2116), (1, 1), (8, 64)])
+@pytest.mark.parametrize("where", ["device", "host"])
+def test_decode_attention(G, k, where):
+    from fathom_b200.offload import MappedBuffer, decode_attention
+    BH, cap = 4, 30000
+    K, V = _kv(BH, cap, G * 1000 + k)
+    g = torch.Generator().manual_seed(k)
+    q = torch.randn(BH, G, 128, generator=g)
+    idx = torch.randint(0, cap, (BH, G, k), generator=g)
+    idx[:, :, : k // 3] = idx[:, :1, : k // 3]                  # shared picks across the GQA group
+    if where == "device":
+        Ks, Vs = K.cuda(), V.cuda()
+    else:
+        kb, vb = MappedBuffer(K.shape, torch.bfloat16), MappedBuffer(V.shape, torch.bfloat16)
+        kb.host.copy_(K)
+        vb.host.copy_(V)
+        Ks, Vs = kb.dev, vb.dev
+    out = decode_attention(q.cuda(), idx.cuda(), Ks, Vs, cap).cpu().numpy()
+    ref = O.decode_attention(q.numpy(), O.bf16_to_f32(K.view(torch.int16).numpy().view(np.uint16)),
+                             O.bf16_to_f32(V.view(torch.int16).numpy().view(np.uint16)), idx.numpy())
+    assert np.abs(out - ref).max() <= 1e-5 * np.abs(ref).max() + 1e-6
+    outb = decode_attention(q.cuda(), idx.cuda(), Ks, Vs, cap, out_dtype=torch.bfloat16).float().cpu().numpy()
+    assert np.abs(outb - ref).max() <= 1e-2 * np.abs(ref).max()
+
+
+def test_decode_attention_recent_rows():
+    """Indices >= n_host read the device-resident recent buffer (offload_attn :234-241)."""
+    from fathom_b200.offload import decode_attention
+    BH, G, k, cap, n_host, rc = 2, 4, 100, 2000, 1990, 16
+    K, V = _kv(BH, cap, 5)
+    Kr, Vr = _kv(BH, rc, 6)
+    idx = torch.randint(0, n_host + rc, (BH, G, k))
+    q = torch.randn(BH, G, 128)
+    out = decode_attention(q.cuda(), idx.cuda(), K.cuda(), V.cuda(), cap, n_host, Kr.cuda(), Vr.cuda(), rc)
+    f = lambda t: O.bf16_to_f32(t.view(torch.int16).numpy().view(np.uint16))
+    ref = O.decode_attention(q.numpy(), f(K), f(V), idx.numpy(), f(Kr), f(Vr), n_host)
+    assert np.abs(out.cpu().numpy() - ref).max() <= 1e-5 * np.abs(ref).max() + 1e-6

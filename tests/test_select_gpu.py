@@ -1,0 +1,103 @@
+"""Top-k selection on the GPU: sink_local_topk, select_topk and merge_topk against the oracle
+(exact, including the deterministic tie order) and the reference's fixtures (sets up to ties)."""
+import numpy as np
+import pytest
+import torch
+
+from oracle import bitplane_oracle as O
+from tests.helpers import CASES, load, topk_sets_agree
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.mark.parametrize("name", [c for c in CASES if c != "s4_b0"])
+def test_sink_local_topk_golden(name):
+    from fathom_b200 import bitplane as bp
+    z = load(name)
+    k, sink, local = int(z["topk_k"]), int(z["topk_sink"]), int(z["topk_local"])
+    idx = bp.sink_local_topk(torch.from_numpy(z["scores"]).cuda(), k, sink, local).cpu().numpy()
+    kk = k - sink - local
+    masked = z["scores"].copy()
+    masked[..., :sink] = -np.inf
+    masked[..., masked.shape[-1] - local:] = -np.inf
+    assert topk_sets_agree(masked, idx, z["topk"], kk)
+    assert np.array_equal(idx[..., kk:], z["topk"][..., kk:])
+    assert np.array_equal(idx, O.sink_local_topk(z["scores"], k, sink, local))
+
+
+@pytest.mark.parametrize("rows,n,k,sink,local", [(32, 131072, 580, 4, 64), (8, 16384, 580, 4, 64), (3, 1000, 1000, 0, 0),
+                                                 (5, 777, 1, 0, 0), (4, 70000, 2116, 4, 64), (2, 300000, 4096, 0, 0)])
+def test_sink_local_topk_random_exact(rows, n, k, sink, local):
+    from fathom_b200 import bitplane as bp
+    g = torch.Generator().manual_seed(n + k)
+    s = torch.randn(rows, n, generator=g)
+    idx = bp.sink_local_topk(s.cuda(), k, sink, local).cpu().numpy()
+    assert np.array_equal(idx, O.sink_local_topk(s.numpy(), k, sink, local))
+
+
+@pytest.mark.parametrize("levels", [1, 3, 50, 5000])
+def test_ties_follow_index_order(levels):
+    """Heavy ties (few distinct values; `levels=1` is an all-equal row that forces the exact
+    whole-row path): the result is the oracle's (score desc, index asc) order exactly."""
+    from fathom_b200 import bitplane as bp
+    g = torch.Generator().manual_seed(levels)
+    s = torch.randint(0, levels, (6, 40000), generator=g).float()
+    idx = bp.sink_local_topk(s.cuda(), 600, 4, 64).cpu().numpy()
+    assert np.array_equal(idx, O.sink_local_topk(s.numpy(), 600, 4, 64))
+
+
+def test_select_topk_offset_mask_scores():
+    from fathom_b200 import bitplane as bp
+    g = torch.Generator().manual_seed(1)
+    s = torch.randn(4, 9000, generator=g)
+    idx, vals = bp.select_topk(s.cuda(), 300, mask_lo=10, mask_hi=8000, index_offset=123456, with_scores=True)
+    m = s.numpy().copy()
+    m[:, :10] = -np.inf
+    m[:, 8000:] = -np.inf
+    ref = O.topk_desc(m, 300)
+    assert np.array_equal(idx.cpu().numpy(), ref + 123456)
+    assert np.array_equal(vals.cpu().numpy(), np.take_along_axis(m, ref, -1))
+
+
+def test_select_with_neg_inf_and_small_rows():
+    """kk larger than the unmasked count: masked (-inf) tokens fill the tail in index order."""
+    from fathom_b200 import bitplane as bp
+    s = torch.randn(3, 50)
+    idx = bp.select_topk(s.cuda(), 20, mask_lo=5, mask_hi=15).cpu().numpy()
+    m = s.numpy().copy()
+    m[:, :5] = -np.inf
+    m[:, 15:] = -np.inf
+    assert np.array_equal(idx, O.topk_desc(m, 20))
+
+
+@pytest.mark.parametrize("m,kk", [(4096, 512), (2048, 2048), (8192, 100), (3, 2)])
+def test_merge_topk(m, kk):
+    from fathom_b200 import bitplane as bp
+    g = torch.Generator().manual_seed(m)
+    cs = torch.randn(7, m, generator=g)
+    half = m // 2
+    cs[:, half:2 * half] = cs[:, :half]                     # duplicate scores: tie order by index
+    ci = torch.randperm(1 << 22, generator=g)[: 7 * m].view(7, m)
+    idx, vals = bp.merge_topk(cs.cuda(), ci.cuda(), kk)
+    ref = O.merge_candidates(cs.numpy(), ci.numpy(), kk)
+    assert np.array_equal(idx.cpu().numpy(), ref)
+
+
+def test_shard_merge_equals_single():
+    """Context split into 4 chunks: per-chunk select (global indices) + merge == single-pass select."""
+    from fathom_b200 import bitplane as bp
+    g = torch.Generator().manual_seed(7)
+    n, kk, sink, local = 40000, 512, 4, 64
+    s = torch.randn(8, n, generator=g).cuda()
+    full = bp.select_topk(s, kk, mask_lo=sink, mask_hi=n - local)
+    bounds = [0, 9984, 20032, 30016, n]                       # 64-token aligned boundaries
+    cs, ci = [], []
+    for r in range(4):
+        a, b = bounds[r], bounds[r + 1]
+        lo = max(sink - a, 0)
+        hi = min(n - local, b) - a
+        i, v = bp.select_topk(s[:, a:b], kk, mask_lo=lo, mask_hi=max(hi, 0), index_offset=a, with_scores=True)
+        cs.append(v)
+        ci.append(i)
+    idx, _ = bp.merge_topk(torch.cat(cs, -1), torch.cat(ci, -1), kk)
+    assert torch.equal(idx, full)
