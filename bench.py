@@ -1,0 +1,441 @@
+#!/usr/bin/env python
+"""Benchmark of the Fathom key-scan decode step on B200.
+
+Headline workload: Qwen3-8B attention shape (8 KV heads, G=4, D=128),
+batch 1, T = 1,048,576 tokens, 36 layers, budget 48 (the paper's 56-bit "Fathom 48"),
+k = 512 + 4 sink + 64 local.  The bit-plane index (copy-index order) and the bf16 K/V rows live
+in pinned, mapped host memory.  One step = one decode step = for each of the 36 layers:
+plan -> zero-copy plane-prefix scan of the host index -> sink+local top-k -> unique-row
+zero-copy gather + exact attention.  Layers run back to back on one stream (a layer's query
+depends on the previous layer's output in a real model).
+
+  value   scanned key-rows/s = T * Hkv * layers / step time, inputs (q, g) already on the device
+  e2e     the same through the public API with host buffers: every step copies that step's
+          queries and gains from pinned host memory and reads the attention outputs back
+  roofline  the scan kernel: algorithmic bytes (bytes_planes of each layer's plan) / its mean
+          CUDA-event duration, against the host link bandwidth measured in this run (pinned
+          H2D cudaMemcpy, 1 GiB)
+  hbm_resident  config 1 (T = 131072, index + K/V in HBM) as a secondary figure, against
+          MEASURED_PEAKS.json hbm_gbs
+  cpu_baseline  the CPU oracle (numpy restatement of the reference path) on a bounded sample
+
+`--impl reference` times the reference's CPU path (the oracle port; the reference is Python and
+its checkout is not on the GPU box) on bounded samples of the same workload.
+Multi-GPU (torchrun, N > 1): the context is split into contiguous 64-token-aligned chunks of T
+tokens per rank (weak scaling: N*T total); each rank scans its chunk, keeps its local top-k, and
+an NCCL all-gather plus a merge produce the global top-k; attention partials are combined the
+same way.
+"""
+import argparse
+import json
+import math
+import os
+import subprocess
+import sys
+import time
+
+import numpy as np
+import torch
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, REPO)
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["fathom", "reference"], default="fathom")
+    ap.add_argument("--ctx", type=int, default=1048576, help="tokens per rank")
+    ap.add_argument("--layers", type=int, default=36)
+    ap.add_argument("--kv-buffers", type=int, default=4, help="distinct host K/V row buffers, cycled over layers")
+    ap.add_argument("--hkv", type=int, default=8)
+    ap.add_argument("--g", type=int, default=4)
+    ap.add_argument("--budget", type=float, default=48.0)
+    ap.add_argument("--k", type=int, default=512)
+    ap.add_argument("--sink", type=int, default=4)
+    ap.add_argument("--local", type=int, default=64)
+    ap.add_argument("--hbm-ctx", type=int, default=131072)
+    ap.add_argument("--no-hbm", action="store_true", help="skip the HBM-resident secondary figure")
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
+    ap.add_argument("--cpu-heads", type=int, default=2, help="KV heads of one layer in the CPU sample")
+    return ap.parse_args()
+
+
+def log(*a):
+    print(*a, file=sys.stderr, flush=True)
+
+
+# ------------------------------------------------------------------ clocks
+class Clocks:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.proc = None
+        self.path = os.path.join(REPO, "gpurun_out", f"clocks_bench_{os.getpid()}.csv")
+
+    def start(self):
+        try:
+            os.makedirs(os.path.dirname(self.path), exist_ok=True)
+            self.f = open(self.path, "w")
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"], stdout=self.f,
+                                         stderr=subprocess.DEVNULL)
+        except Exception as e:  # nvidia-smi missing: report no clocks
+            log("clock sampling unavailable:", e)
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        self.f.close()
+        rows = []
+        for line in open(self.path):
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) >= 8 and parts[1].replace(".", "").isdigit():
+                rows.append(parts)
+        if not rows:
+            return None
+        sm = [float(r[1]) for r in rows]
+        mx = float(rows[0][2])
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[4 + i].lower() == "active"})
+        return {"sm_mhz": float(np.median(sm)), "sm_max_mhz": mx, "reasons": reasons, "samples": len(rows),
+                "power_w_max": max(float(r[3]) for r in rows if r[3].replace(".", "").isdigit())}
+
+
+# ------------------------------------------------------------------ helpers
+def measured_peaks():
+    p = os.path.join(REPO, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return d, "measured"
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}, "fallback"
+
+
+def host_link_gbs(dev):
+    """Pinned host -> device cudaMemcpy bandwidth (1 GiB, best of 5): the host-link roofline."""
+    n = 1 << 30
+    h = torch.empty(n, dtype=torch.uint8, pin_memory=True)
+    d = torch.empty(n, dtype=torch.uint8, device=dev)
+    best = 0.0
+    for _ in range(6):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        d.copy_(h, non_blocking=True)
+        e1.record()
+        torch.cuda.synchronize()
+        best = max(best, n / (e0.elapsed_time(e1) * 1e-3) / 1e9)
+    del h, d
+    return best
+
+
+class Layer:
+    pass
+
+
+def build_host_layers(a, dev, rank, world, bp, off):
+    """Per layer: a host-order store of this rank's context chunk in mapped host memory, the layer's
+    query and gain on the device; K/V row buffers for the first kv_buffers layers."""
+    from fathom_b200.synth import make_layer
+    layers, kv = [], []
+    BH = a.hkv
+    for L in range(a.layers):
+        gen = torch.Generator(device=dev).manual_seed(1000 * (rank + 1) + L)
+        qgen = torch.Generator(device=dev).manual_seed(777 + L)     # same query on every rank
+        scale = torch.randn(BH, 1, 128, generator=qgen, device=dev).exp()
+        q = torch.randn(BH, a.g, 128, generator=qgen, device=dev) * scale
+        K = (torch.randn(BH, a.ctx, 128, generator=gen, device=dev) * scale).to(torch.bfloat16)
+        lay = Layer()
+        lay.q = q.contiguous()
+        lay.g = ((q ** 2) * (scale[:, 0, None, :] ** 2)).sum(1).contiguous()   # Var(K) = scale^2 (same on all ranks)
+        lay.store = off.HostPlaneStore(K)
+        plan = bp.make_plan(lay.g, a.budget)
+        lay.bytes = bp.bytes_planes(plan["t"], a.ctx)
+        lay.nact = float(plan["nact"].float().mean())
+        if L < a.kv_buffers:
+            V = (torch.randn(BH, a.ctx, 128, generator=gen, device=dev) * scale).to(torch.bfloat16)
+            kb = off.MappedBuffer(K.shape, torch.bfloat16, dev)
+            vb = off.MappedBuffer(V.shape, torch.bfloat16, dev)
+            kb.dev.copy_(K)
+            vb.dev.copy_(V)
+            kv.append((kb, vb))
+            del V
+        del K
+        torch.cuda.synchronize(dev)
+        layers.append(lay)
+    return layers, kv
+
+
+def decode_step_1gpu(a, layers, kv, bp, off, scores, outs, q_in=None, g_in=None, scan_events=None):
+    """One decode step over all layers (device-resident q/g unless q_in/g_in given)."""
+    k_tot = a.k + a.sink + a.local
+    for L, lay in enumerate(layers):
+        q = lay.q if q_in is None else q_in[L]
+        g = lay.g if g_in is None else g_in[L]
+        plan = bp.make_plan(g, a.budget)
+        if scan_events is not None:
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+        s = lay.store.scan(q, plan, out=scores)
+        if scan_events is not None:
+            e1.record()
+            scan_events.append((e0, e1, lay.bytes))
+        idx = bp.sink_local_topk(s, k_tot, a.sink, a.local)
+        kb, vb = kv[L % len(kv)]
+        outs[L] = off.decode_attention(q, idx, kb.dev, vb.dev, a.ctx)
+    return outs
+
+
+# ------------------------------------------------------------------ CPU baseline (oracle port)
+def cpu_sample(a, heads, seed_layer=0):
+    """The reference path on the host cores (numpy oracle, all BLAS threads): plan + scan +
+    sink_local_topk + gather/attention for `heads` KV heads of one layer at T = a.ctx.
+    Returns (seconds, key-rows)."""
+    from oracle import bitplane_oracle as O
+    g = torch.Generator().manual_seed(4242 + seed_layer)
+    scale = torch.randn(heads, 1, 128, generator=g).exp()
+    K = (torch.randn(heads, a.ctx, 128, generator=g) * scale).to(torch.bfloat16).float().numpy()
+    V = (torch.randn(heads, a.ctx, 128, generator=g) * scale).to(torch.bfloat16).float().numpy()
+    q = (torch.randn(heads, a.g, 128, generator=g) * scale).numpy()
+    gain = ((q ** 2) * (scale[:, 0].numpy() ** 2)[:, None, :]).sum(1)
+    code, sc = O.quantise_u4(K)               # offline store build: not timed
+    k_tot = a.k + a.sink + a.local
+    t0 = time.perf_counter()
+    plan = O.make_plan(gain, a.budget)
+    s = O.scan_scores(q, code, sc, plan["t"])
+    idx = O.sink_local_topk(s, k_tot, a.sink, a.local)
+    O.decode_attention(q, K, V, idx)
+    return time.perf_counter() - t0, heads * a.ctx
+
+
+def run_reference(a, rank, world):
+    """--impl reference: rank 0 times the CPU reference path (oracle port) per step on a bounded
+    sample; other ranks exit without work."""
+    if rank != 0:
+        return
+    cores = os.cpu_count()
+    for _ in range(a.warmup):
+        cpu_sample(a, 1)
+    ts, rows = [], 0
+    for s in range(a.steps):
+        t, r = cpu_sample(a, 1, seed_layer=s)
+        ts.append(t)
+        rows = r
+    tmean = float(np.mean(ts))
+    val = rows / tmean
+    sample = (f"1 KV head x {a.ctx} tokens of one layer per step (plan+scan+sink_local_topk+attention), "
+              f"numpy oracle, {cores} threads; scaled to key-rows/s")
+    line = {"impl": "reference", "metric": METRIC, "value": val, "unit": "key-rows/s", "n_gpus": world,
+            "steps": a.steps, "warmup": a.warmup, "ms_per_step": tmean * 1e3, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": config_dict(a, world),
+            "cpu_baseline": {"value": val, "unit": "key-rows/s", "cores": cores, "kind": "port", "sample": sample},
+            "e2e": {"value": val, "unit": "key-rows/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+METRIC = "scanned key-rows/s and decode-step us at 1M ctx, 56-bit, k=512 (1/2/4/8 GPU)"
+
+
+def config_dict(a, world):
+    return {"workload": "config2: host-resident index + K/V rows, Qwen3-8B attention shape, decode step",
+            "ctx_per_gpu": a.ctx, "ctx_total": a.ctx * world, "layers": a.layers, "kv_heads": a.hkv,
+            "q_per_kv": a.g, "head_dim": 128, "batch": 1, "budget": a.budget, "k": a.k, "sink": a.sink,
+            "local": a.local, "kv_row_buffers": a.kv_buffers,
+            "parallelism": "context-shard" + str(world) if world > 1 else "single",
+            "l2": "inputs larger than L2 (host index per step >> 126 MB)"}
+
+
+# ------------------------------------------------------------------ HBM-resident secondary figure
+def hbm_figure(a, dev, bp, off, peaks):
+    from fathom_b200.synth import make_layer
+    n = a.hbm_ctx
+    layers, kvs = [], []
+    for L in range(a.layers):
+        d = make_layer(a.hkv, a.g, n, seed=1, layer=L, device=dev, kv_dtype=torch.bfloat16, with_v=True)
+        lay = Layer()
+        lay.store = bp.PlaneStore(d["K"])
+        lay.q, lay.g = d["q"], d["g"]
+        lay.bytes = bp.bytes_planes(bp.make_plan(d["g"], a.budget)["t"], n)
+        kvs.append((d["K"], d["V"]))
+        layers.append(lay)
+    k_tot = a.k + a.sink + a.local
+    scores = torch.empty(a.hkv, a.g, n, device=dev)
+
+    def step(ev=None):
+        for L, lay in enumerate(layers):
+            plan = bp.make_plan(lay.g, a.budget)
+            if ev is not None:
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record()
+            s = lay.store.scan(lay.q, plan, out=scores)
+            if ev is not None:
+                e1.record()
+                ev.append((e0, e1, lay.bytes))
+            idx = bp.sink_local_topk(s, k_tot, a.sink, a.local)
+            off.decode_attention(lay.q, idx, kvs[L][0], kvs[L][1], n)
+
+    for _ in range(a.warmup):
+        step()
+    torch.cuda.synchronize()
+    # graph of the whole step removes the per-launch host cost from the per-layer latency
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        step()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(a.steps):
+        g.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / a.steps
+    ev = []
+    for _ in range(2):
+        step(ev)
+    torch.cuda.synchronize()
+    durs = [x.elapsed_time(y) for x, y, _ in ev]
+    byts = [b for _, _, b in ev]
+    scan_ms = float(np.mean(durs))
+    achieved = float(np.mean(byts)) / (scan_ms * 1e-3) / 1e9
+    rows = n * a.hkv * a.layers
+    del g
+    return {"workload": "config1: HBM-resident index + K/V, T=131072, 36 layers, graph-captured step",
+            "value": rows / (ms * 1e-3), "unit": "key-rows/s", "ms_per_step": ms,
+            "scan_ms_per_layer": scan_ms,
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                         "frac": achieved / peaks["hbm_gbs"], "traffic": None,
+                         "bytes_per_launch": float(np.mean(byts))},
+            "bits_per_row": float(np.mean(byts)) * 8 / (n * a.hkv)}
+
+
+# ------------------------------------------------------------------ main
+def main():
+    a = parse()
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if a.impl == "reference":
+        run_reference(a, rank, world)
+        return
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    if world > 1:
+        import datetime
+        torch.distributed.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=300))
+    from fathom_b200 import bitplane as bp
+    from fathom_b200 import offload as off
+    from fathom_b200 import _lib
+    _lib.lib()
+    peaks, peaks_kind = measured_peaks()
+
+    link = host_link_gbs(dev)
+    log(f"[rank {rank}] host link H2D {link:.1f} GB/s")
+    t0 = time.time()
+    layers, kv = build_host_layers(a, dev, rank, world, bp, off)
+    log(f"[rank {rank}] built {a.layers} host layers in {time.time() - t0:.1f} s")
+    scores = torch.empty(a.hkv, a.g, a.ctx, device=dev)
+    outs = [None] * a.layers
+
+    if world > 1:
+        from fathom_b200 import shard
+        step_fn = lambda q_in=None, g_in=None, ev=None: shard.sharded_decode_step(
+            a, layers, kv, scores, outs, rank, world, q_in=q_in, g_in=g_in, scan_events=ev)
+    else:
+        step_fn = lambda q_in=None, g_in=None, ev=None: decode_step_1gpu(
+            a, layers, kv, bp, off, scores, outs, q_in=q_in, g_in=g_in, scan_events=ev)
+
+    def barrier():
+        if world > 1:
+            torch.distributed.barrier()
+        torch.cuda.synchronize(dev)
+
+    for _ in range(a.warmup):
+        step_fn()
+    barrier()
+    clocks = Clocks(local_rank)
+    clocks.start()
+    ev = []
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(a.steps):
+        step_fn(ev=ev)
+    e1.record()
+    barrier()
+    ms = e0.elapsed_time(e1) / a.steps
+
+    # e2e through the public API with host buffers: H2D of the step's q/g, D2H of the outputs
+    q_host = torch.stack([l.q for l in layers]).cpu().pin_memory()
+    g_host = torch.stack([l.g for l in layers]).cpu().pin_memory()
+    out_host = torch.empty(a.layers, a.hkv, a.g, 128, pin_memory=True)
+    q_dev = torch.empty_like(q_host, device=dev)
+    g_dev = torch.empty_like(g_host, device=dev)
+    barrier()
+    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    f0.record()
+    for _ in range(a.steps):
+        q_dev.copy_(q_host, non_blocking=True)
+        g_dev.copy_(g_host, non_blocking=True)
+        step_fn(q_in=q_dev, g_in=g_dev)
+        out_host.copy_(torch.stack(outs), non_blocking=True)
+    f1.record()
+    barrier()
+    clk = clocks.stop()
+    e2e_ms = f0.elapsed_time(f1) / a.steps
+
+    if world > 1:
+        t = torch.tensor([ms, e2e_ms], device=dev)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        ms, e2e_ms = t.tolist()
+    rows_step = a.ctx * world * a.hkv * a.layers
+    durs = [x.elapsed_time(y) for x, y, _ in ev]
+    byts = [b for _, _, b in ev]
+    scan_ms = float(np.mean(durs))
+    achieved = float(np.mean(byts)) / (scan_ms * 1e-3) / 1e9
+    bits_row = float(np.mean(byts)) * 8 / (a.ctx * a.hkv)
+    launches_per_layer = 7 if world == 1 else 8
+    line = {"metric": METRIC, "value": rows_step / (ms * 1e-3), "unit": "key-rows/s", "n_gpus": world,
+            "steps": a.steps, "warmup": a.warmup, "ms_per_step": ms, "decode_step_us": ms * 1e3,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (seeded lognormal-channel keys/values/queries)", "config": config_dict(a, world),
+            "bits_per_row": bits_row,
+            "roofline": {"bound": "host_link", "achieved": achieved, "peak": link, "unit": "GB/s",
+                         "frac": achieved / link, "traffic": None,
+                         "bytes_per_launch": float(np.mean(byts)),
+                         "kernel": "scan (zero-copy reads of the host index)",
+                         "peak_source": "pinned H2D cudaMemcpy of 1 GiB measured in this run"},
+            "scan_ms_per_layer": scan_ms,
+            "e2e": {"value": rows_step / (e2e_ms * 1e-3), "unit": "key-rows/s", "ms_per_step": e2e_ms,
+                    "h2d_bytes_per_step": q_host.numel() * 4 + g_host.numel() * 4,
+                    "d2h_bytes_per_step": out_host.numel() * 4},
+            "gpu_launches": launches_per_layer * a.layers * a.steps,
+            "clocks": clk, "peaks_source": peaks_kind}
+    if rank == 0 and world == 1 and not a.no_hbm:
+        del layers, kv
+        torch.cuda.empty_cache()
+        line["hbm_resident"] = hbm_figure(a, dev, bp, off, peaks)
+    if rank == 0 and world == 1 and not a.no_cpu:
+        t, r = cpu_sample(a, a.cpu_heads)
+        line["cpu_baseline"] = {"value": r / t, "unit": "key-rows/s", "cores": os.cpu_count(), "kind": "port",
+                                "sample": f"{a.cpu_heads} KV heads x {a.ctx} tokens of one layer: plan+scan+"
+                                          f"sink_local_topk+attention, numpy oracle ({t:.1f} s)"}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        torch.distributed.barrier()
+        torch.distributed.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

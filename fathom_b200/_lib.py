@@ -42,6 +42,9 @@ SIGNATURES = {
     "fathom_gather_rows": (I32, [P, I64, P, I64, I64, I64, P, P]),
     "fathom_decode_workspace_bytes": (SZ, [I64, I32, I64]),
     "fathom_decode_attention": (I32, [P, I64, I32, P, I64, P, P, I64, I64, P, P, I64, P, P, P, SZ, P]),
+    "fathom_decode_partial_workspace_bytes": (SZ, [I64, I32, I64]),
+    "fathom_decode_attention_partial": (I32, [P, I64, I32, P, I64, P, P, I64, I64, I64, P, P, SZ, P]),
+    "fathom_attention_combine": (I32, [P, I64, I64, P, P, P]),
     "fathom_host_alloc_mapped": (I32, [SZ, ctypes.POINTER(P), ctypes.POINTER(P)]),
     "fathom_host_free": (I32, [P]),
 }

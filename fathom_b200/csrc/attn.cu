@@ -96,6 +96,7 @@ __device__ uint32_t block_exclusive_scan(uint32_t v, uint32_t* s_warp, uint32_t*
 constexpr int POS_BITS = 24;  // position of a pick within G*k (< 2^24); index in the upper 40 bits
 
 __global__ void __launch_bounds__(DT) dedupe_gather_kernel(const int64_t* __restrict__ idx, int64_t M,
+                                                           int64_t idx_lo, int64_t idx_hi,
                                                            const uint4* __restrict__ ksrc, const uint4* __restrict__ vsrc,
                                                            int64_t cap, int64_t n_host, const uint4* __restrict__ krec,
                                                            const uint4* __restrict__ vrec, int64_t recent_cap,
@@ -128,8 +129,10 @@ __global__ void __launch_bounds__(DT) dedupe_gather_kernel(const int64_t* __rest
     uint32_t tot;
     const uint32_t ex = block_exclusive_scan(first ? 1u : 0u, s_warp, &tot);
     if (i < M) {
-      sl[v & ((1ull << POS_BITS) - 1)] = (int32_t)(base + ex - (first ? 0u : 1u));
-      if (first) ul[base + ex] = (int64_t)(v >> POS_BITS);
+      const int64_t t = (int64_t)(v >> POS_BITS);
+      const bool owned = t >= idx_lo && t < idx_hi;
+      sl[v & ((1ull << POS_BITS) - 1)] = owned ? (int32_t)(base + ex - (first ? 0u : 1u)) : -1;
+      if (first) ul[base + ex] = owned ? t - idx_lo : -1;
     }
     base += tot;
   }
@@ -147,8 +150,8 @@ __global__ void __launch_bounds__(DT) dedupe_gather_kernel(const int64_t* __rest
 #pragma unroll
     for (int u = 0; u < UNROLL; ++u) {
       const int64_t r = r0 + (int64_t)u * rows_per_iter;
-      if (r < U) {
-        const int64_t t = ul[r];
+      const int64_t t = r < U ? ul[r] : -1;
+      if (t >= 0) {
         const uint4* kp;
         const uint4* vp;
         if (t < n_host) {
@@ -165,7 +168,7 @@ __global__ void __launch_bounds__(DT) dedupe_gather_kernel(const int64_t* __rest
 #pragma unroll
     for (int u = 0; u < UNROLL; ++u) {
       const int64_t r = r0 + (int64_t)u * rows_per_iter;
-      if (r < U) {
+      if (r < U && ul[r] >= 0) {
         ks[r * LPR + sub] = kv[u];
         vs[r * LPR + sub] = vv[u];
       }
@@ -179,7 +182,7 @@ __device__ __forceinline__ float bf16hi(uint32_t w) { return __uint_as_float(w &
 __global__ void __launch_bounds__(AT) attend_kernel(const float* __restrict__ q, int G, int64_t k, int64_t M,
                                                     const int32_t* __restrict__ slot, const uint16_t* __restrict__ kstage,
                                                     const uint16_t* __restrict__ vstage, float* __restrict__ out_f32,
-                                                    uint16_t* __restrict__ out_bf16) {
+                                                    uint16_t* __restrict__ out_bf16, float* __restrict__ out_ml) {
   extern __shared__ float s_p[];  // k probabilities
   __shared__ float s_q[D];
   __shared__ float s_red[AT / 32];
@@ -199,9 +202,13 @@ __global__ void __launch_bounds__(AT) attend_kernel(const float* __restrict__ q,
   for (int i = 0; i < 4; ++i) qv[i] = s_q[lane * 4 + i];
   float mloc = -INFINITY;
   for (int64_t r = warp; r < k; r += AT / 32) {
-    const uint2 w = *reinterpret_cast<const uint2*>(kb + (int64_t)sl[r] * D + lane * 4);
-    float d = qv[0] * bf16lo(w.x) + qv[1] * bf16hi(w.x) + qv[2] * bf16lo(w.y) + qv[3] * bf16hi(w.y);
-    d = warp_sum(d) * scale;
+    const int32_t sr = sl[r];
+    float d = -INFINITY;
+    if (sr >= 0) {  // slot -1: the pick is owned by another context shard
+      const uint2 w = *reinterpret_cast<const uint2*>(kb + (int64_t)sr * D + lane * 4);
+      d = qv[0] * bf16lo(w.x) + qv[1] * bf16hi(w.x) + qv[2] * bf16lo(w.y) + qv[3] * bf16hi(w.y);
+      d = warp_sum(d) * scale;
+    }
     if (lane == 0) s_p[r] = d;
     mloc = fmaxf(mloc, d);
   }
@@ -213,7 +220,7 @@ __global__ void __launch_bounds__(AT) attend_kernel(const float* __restrict__ q,
   __syncthreads();
   float sloc = 0.0f;
   for (int64_t r = tid; r < k; r += AT) {
-    const float e = expf(s_p[r] - m);
+    const float e = s_p[r] == -INFINITY ? 0.0f : expf(s_p[r] - m);
     s_p[r] = e;
     sloc += e;
   }
@@ -227,16 +234,58 @@ __global__ void __launch_bounds__(AT) attend_kernel(const float* __restrict__ q,
   const int dim = tid & (D - 1), par = tid >> 7;
   float acc = 0.0f;
   for (int64_t r = par; r < k; r += 2) {
-    const uint16_t v = vb[(int64_t)sl[r] * D + dim];
-    acc = fmaf(s_p[r], __uint_as_float((uint32_t)v << 16), acc);
+    const int32_t sr = sl[r];
+    if (sr >= 0) {
+      const uint16_t v = vb[(int64_t)sr * D + dim];
+      acc = fmaf(s_p[r], __uint_as_float((uint32_t)v << 16), acc);
+    }
   }
   s_acc[par][dim] = acc;
   __syncthreads();
   if (tid < D) {
-    const float o = (s_acc[0][tid] + s_acc[1][tid]) / ssum;
-    if (out_f32) out_f32[bhg * D + tid] = o;
-    if (out_bf16) out_bf16[bhg * D + tid] = __bfloat16_as_ushort(__float2bfloat16_rn(o));
+    const float un = s_acc[0][tid] + s_acc[1][tid];
+    if (out_ml) {  // partial: unnormalised sum, with (max, sum of exp) beside it
+      out_f32[bhg * D + tid] = un;
+      if (tid == 0) {
+        out_ml[bhg * 2] = m;
+        out_ml[bhg * 2 + 1] = ssum;
+      }
+    } else {
+      const float o = un / ssum;
+      if (out_f32) out_f32[bhg * D + tid] = o;
+      if (out_bf16) out_bf16[bhg * D + tid] = __bfloat16_as_ushort(__float2bfloat16_rn(o));
+    }
   }
+}
+
+// out = sum_p o_p e^(m_p - M) / sum_p l_p e^(m_p - M), M = max_p m_p: log-sum-exp merge of the
+// partial attention of P context shards.  One CTA of 128 threads per (batch, query head).
+__global__ void __launch_bounds__(D) combine_kernel(const float* __restrict__ parts, int64_t P, int64_t rows,
+                                                    float* __restrict__ out_f32, uint16_t* __restrict__ out_bf16) {
+  const int64_t row = blockIdx.x;
+  const int t = threadIdx.x;
+  constexpr int W = D + 2;  // packed part: o[128], m, l
+  float M = -INFINITY;
+  for (int64_t p = 0; p < P; ++p) M = fmaxf(M, parts[(p * rows + row) * W + D]);
+  float L = 0.0f, acc = 0.0f;
+  for (int64_t p = 0; p < P; ++p) {
+    const float* pp = parts + (p * rows + row) * W;
+    const float m = pp[D];
+    const float w = m == -INFINITY ? 0.0f : expf(m - M);
+    L = fmaf(pp[D + 1], w, L);
+    acc = fmaf(pp[t], w, acc);
+  }
+  const float o = acc / L;
+  if (out_f32) out_f32[row * D + t] = o;
+  if (out_bf16) out_bf16[row * D + t] = __bfloat16_as_ushort(__float2bfloat16_rn(o));
+}
+
+__global__ void pack_partial_kernel(const float* __restrict__ o, const float* __restrict__ ml, int64_t rows,
+                                    float* __restrict__ packed) {
+  const int64_t row = blockIdx.x;
+  const int t = threadIdx.x;
+  packed[row * (D + 2) + t] = o[row * D + t];
+  if (t < 2) packed[row * (D + 2) + D + t] = ml[row * 2 + t];
 }
 
 __global__ void gather_rows_kernel(const uint4* __restrict__ src, int64_t cap, const int32_t* __restrict__ idx,
@@ -249,6 +298,41 @@ __global__ void gather_rows_kernel(const uint4* __restrict__ src, int64_t cap, c
   const int32_t t = idx[bh * R + r];
   if (t < 0) return;
   dst[(bh * R + r) * lpr + sub] = src[(bh * cap + t) * lpr + sub];
+}
+
+
+int run_decode(const float* q, int64_t BH, int G, const int64_t* idx, int64_t k, const uint16_t* K_src,
+               const uint16_t* V_src, int64_t cap, int64_t n_host, const uint16_t* K_recent, const uint16_t* V_recent,
+               int64_t recent_cap, int64_t idx_lo, int64_t idx_hi, float* out_f32, uint16_t* out_bf16,
+               float* out_ml, void* workspace, size_t workspace_bytes, cudaStream_t st) {
+  FATHOM_REQUIRE(q && idx && K_src && V_src && workspace, FATHOM_ERR_NULL, "decode_attention: NULL pointer");
+  FATHOM_REQUIRE(out_f32 || out_bf16, FATHOM_ERR_NULL, "decode_attention: no output");
+  FATHOM_REQUIRE(BH >= 1 && G >= 1 && k >= 1 && n_host >= 0 && n_host <= cap && idx_lo <= idx_hi, FATHOM_ERR_SHAPE,
+                 "decode_attention: bad shape");
+  const int64_t M = (int64_t)G * k;
+  FATHOM_REQUIRE(M <= MAX_M, FATHOM_ERR_UNSUPPORTED, "decode_attention: G*k=%lld exceeds %d", (long long)M, MAX_M);
+  FATHOM_REQUIRE(recent_cap == 0 || (K_recent && V_recent), FATHOM_ERR_NULL,
+                 "decode_attention: recent buffers missing");
+  FATHOM_REQUIRE(workspace_bytes >= decode_ws_bytes(BH, M) && (reinterpret_cast<uintptr_t>(workspace) & 255) == 0,
+                 FATHOM_ERR_WORKSPACE, "decode_attention: workspace needs %zu bytes, 256-byte aligned",
+                 decode_ws_bytes(BH, M));
+  FATHOM_REQUIRE((reinterpret_cast<uintptr_t>(K_src) & 15) == 0 && (reinterpret_cast<uintptr_t>(V_src) & 15) == 0,
+                 FATHOM_ERR_SHAPE, "decode_attention: K/V sources must be 16-byte aligned");
+  DecodeWs w = carve(workspace, BH, M);
+  int P = 1;
+  while (P < M) P <<= 1;
+  const size_t smem = (size_t)P * sizeof(uint64_t);
+  cudaFuncSetAttribute(dedupe_gather_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  dedupe_gather_kernel<<<(unsigned)BH, DT, smem, st>>>(
+      idx, M, idx_lo, idx_hi, reinterpret_cast<const uint4*>(K_src), reinterpret_cast<const uint4*>(V_src), cap,
+      n_host, reinterpret_cast<const uint4*>(K_recent), reinterpret_cast<const uint4*>(V_recent), recent_cap, w.slot,
+      w.uniq, reinterpret_cast<uint4*>(w.kstage), reinterpret_cast<uint4*>(w.vstage));
+  const size_t smem2 = (size_t)k * sizeof(float);
+  FATHOM_REQUIRE(smem2 <= 160 * 1024, FATHOM_ERR_UNSUPPORTED, "decode_attention: k too large");
+  cudaFuncSetAttribute(attend_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem2);
+  attend_kernel<<<(unsigned)(BH * G), AT, smem2, st>>>(q, G, k, M, w.slot, w.kstage, w.vstage, out_f32, out_bf16,
+                                                       out_ml);
+  return check_launch("decode_attention");
 }
 
 }  // namespace
@@ -266,34 +350,41 @@ extern "C" int fathom_decode_attention(const float* q, int64_t BH, int G, const 
                                        const uint16_t* K_recent, const uint16_t* V_recent, int64_t recent_cap,
                                        float* out_f32, uint16_t* out_bf16, void* workspace, size_t workspace_bytes,
                                        void* stream) {
-  FATHOM_REQUIRE(q && idx && K_src && V_src && workspace, FATHOM_ERR_NULL, "decode_attention: NULL pointer");
-  FATHOM_REQUIRE(out_f32 || out_bf16, FATHOM_ERR_NULL, "decode_attention: no output");
-  FATHOM_REQUIRE(BH >= 1 && G >= 1 && k >= 1 && n_host >= 0 && n_host <= cap, FATHOM_ERR_SHAPE,
-                 "decode_attention: bad shape");
-  const int64_t M = (int64_t)G * k;
-  FATHOM_REQUIRE(M <= MAX_M, FATHOM_ERR_UNSUPPORTED, "decode_attention: G*k=%lld exceeds %d", (long long)M, MAX_M);
-  FATHOM_REQUIRE(recent_cap == 0 || (K_recent && V_recent), FATHOM_ERR_NULL,
-                 "decode_attention: recent buffers missing");
-  FATHOM_REQUIRE(workspace_bytes >= decode_ws_bytes(BH, M) && (reinterpret_cast<uintptr_t>(workspace) & 255) == 0,
-                 FATHOM_ERR_WORKSPACE, "decode_attention: workspace needs %zu bytes, 256-byte aligned",
-                 decode_ws_bytes(BH, M));
-  FATHOM_REQUIRE((reinterpret_cast<uintptr_t>(K_src) & 15) == 0 && (reinterpret_cast<uintptr_t>(V_src) & 15) == 0,
-                 FATHOM_ERR_SHAPE, "decode_attention: K/V sources must be 16-byte aligned");
+  return run_decode(q, BH, G, idx, k, K_src, V_src, cap, n_host, K_recent, V_recent, recent_cap, 0, INT64_MAX,
+                    out_f32, out_bf16, nullptr, workspace, workspace_bytes, reinterpret_cast<cudaStream_t>(stream));
+}
+
+extern "C" int fathom_decode_attention_partial(const float* q, int64_t BH, int G, const int64_t* idx, int64_t k,
+                                               const uint16_t* K_src, const uint16_t* V_src, int64_t cap,
+                                               int64_t idx_lo, int64_t idx_hi, float* out_packed, void* workspace,
+                                               size_t workspace_bytes, void* stream) {
+  FATHOM_REQUIRE(out_packed, FATHOM_ERR_NULL, "decode_attention_partial: NULL output");
+  FATHOM_REQUIRE(idx_hi - idx_lo <= cap, FATHOM_ERR_SHAPE, "decode_attention_partial: owned range exceeds cap");
+  const size_t need = decode_ws_bytes(BH, (int64_t)G * k);
+  const size_t extra = align256((size_t)BH * G * (D + 2) * sizeof(float));
+  FATHOM_REQUIRE(workspace_bytes >= need + extra, FATHOM_ERR_WORKSPACE,
+                 "decode_attention_partial: workspace needs %zu bytes", need + extra);
+  float* o = reinterpret_cast<float*>(static_cast<char*>(workspace) + need);
+  float* ml = o + (size_t)BH * G * D;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-  DecodeWs w = carve(workspace, BH, M);
-  int P = 1;
-  while (P < M) P <<= 1;
-  const size_t smem = (size_t)P * sizeof(uint64_t);
-  cudaFuncSetAttribute(dedupe_gather_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  dedupe_gather_kernel<<<(unsigned)BH, DT, smem, st>>>(
-      idx, M, reinterpret_cast<const uint4*>(K_src), reinterpret_cast<const uint4*>(V_src), cap, n_host,
-      reinterpret_cast<const uint4*>(K_recent), reinterpret_cast<const uint4*>(V_recent), recent_cap, w.slot, w.uniq,
-      reinterpret_cast<uint4*>(w.kstage), reinterpret_cast<uint4*>(w.vstage));
-  const size_t smem2 = (size_t)k * sizeof(float);
-  FATHOM_REQUIRE(smem2 <= 160 * 1024, FATHOM_ERR_UNSUPPORTED, "decode_attention: k too large");
-  cudaFuncSetAttribute(attend_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem2);
-  attend_kernel<<<(unsigned)(BH * G), AT, smem2, st>>>(q, G, k, M, w.slot, w.kstage, w.vstage, out_f32, out_bf16);
-  return check_launch("decode_attention");
+  int r = run_decode(q, BH, G, idx, k, K_src, V_src, cap, idx_hi - idx_lo, nullptr, nullptr, 0, idx_lo, idx_hi, o,
+                     nullptr, ml, workspace, need, st);
+  if (r != FATHOM_OK) return r;
+  pack_partial_kernel<<<(unsigned)(BH * G), D, 0, st>>>(o, ml, BH * G, out_packed);
+  return check_launch("decode_attention_partial");
+}
+
+extern "C" size_t fathom_decode_partial_workspace_bytes(int64_t BH, int G, int64_t k) {
+  if (BH <= 0 || G <= 0 || k <= 0) return 0;
+  return decode_ws_bytes(BH, (int64_t)G * k) + align256((size_t)BH * G * (D + 2) * sizeof(float));
+}
+
+extern "C" int fathom_attention_combine(const float* parts, int64_t P, int64_t rows, float* out_f32, uint16_t* out_bf16,
+                                        void* stream) {
+  FATHOM_REQUIRE(parts && (out_f32 || out_bf16), FATHOM_ERR_NULL, "attention_combine: NULL pointer");
+  FATHOM_REQUIRE(P >= 1 && rows >= 1 && rows <= 0x7fffffffLL, FATHOM_ERR_SHAPE, "attention_combine: bad shape");
+  combine_kernel<<<(unsigned)rows, D, 0, reinterpret_cast<cudaStream_t>(stream)>>>(parts, P, rows, out_f32, out_bf16);
+  return check_launch("attention_combine");
 }
 
 extern "C" int fathom_gather_rows(const uint16_t* src, int64_t cap, const int32_t* idx, int64_t BH, int64_t R, int64_t Dm,

@@ -173,3 +173,32 @@ def decode_step(q, g, budget, store, K_src, V_src, cap, k=580, sink=4, local=64,
     idx = bp.sink_local_topk(s, k, sink, local)
     out = decode_attention(q, idx, K_src, V_src, cap, n_host, K_recent, V_recent, recent_cap, out_dtype)
     return out, idx
+
+
+def decode_attention_partial(q, idx, K_src, V_src, cap, idx_lo, idx_hi):
+    """Attention of one context shard over the picks it owns ([idx_lo, idx_hi), rows idx - idx_lo of
+    K_src/V_src).  Returns packed partials fp32 [BH, G, 130] = (unnormalised output[128], max, sum-exp)."""
+    require_cuda(q, idx)
+    BH, G, D = q.shape
+    k = idx.shape[-1]
+    dev = q.device
+    qc = q.contiguous().float()
+    ic = idx.contiguous().to(torch.int64)
+    out = torch.empty(BH, G, D + 2, device=dev, dtype=torch.float32)
+    ws = _lib.workspace(dev, lib().fathom_decode_partial_workspace_bytes(BH, G, k), "decode_partial")
+    check(lib().fathom_decode_attention_partial(ptr(qc), BH, G, ptr(ic), k, ptr(K_src), ptr(V_src), cap, idx_lo, idx_hi,
+                                                ptr(out), ptr(ws), ws.numel(), stream_of(dev)),
+          "decode_attention_partial")
+    return out
+
+
+def attention_combine(parts, out_dtype=torch.float32):
+    """Log-sum-exp merge of packed partials [P, BH, G, 130] -> [BH, G, 128]."""
+    require_cuda(parts)
+    P, BH, G, W = parts.shape
+    pc = parts.contiguous().float()
+    out = torch.empty(BH, G, W - 2, device=parts.device, dtype=out_dtype)
+    check(lib().fathom_attention_combine(ptr(pc), P, BH * G, ptr(out) if out_dtype == torch.float32 else None,
+                                         ptr(out) if out_dtype == torch.bfloat16 else None,
+                                         stream_of(parts.device)), "attention_combine")
+    return out

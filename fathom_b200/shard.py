@@ -1,0 +1,109 @@
+"""Context-sharded decode step: one process per GPU, the context split into contiguous chunks.
+
+No counterpart in the reference (it runs on one GPU).  Each rank holds the bit-plane index and the
+K/V rows of its chunk (tokens [lo, hi) of n_total) in its own host memory and scans them through its
+own host link.  Per layer:
+
+  1 plan            identical on every rank (same query and gains)
+  2 scan            the rank's chunk
+  3 local select    top-kk of the chunk with the global sink window masked on the rank that holds
+                    it and the global local window masked on the rank(s) that hold it; indices are
+                    global (chunk offset added); the selected scores are kept
+  4 all-gather      (score, index) candidates of every rank (NCCL over NVLink)
+  5 merge           top-kk of the union in (score desc, index asc) order: the global top-kk is
+                    contained in the union of the local top-kk's, so the result equals a single-GPU
+                    selection over the whole context, bit for bit
+  6 attention       each rank attends over the final picks it owns (partial max / sum-exp /
+                    unnormalised output), an all-gather of the partials, and a log-sum-exp combine
+
+Chunk boundaries are multiples of 64 tokens, so every chunk's block scales equal those of the
+single-GPU store.  The per-rank kernels and the collective are parameters so that the host logic
+can be exercised with CPU ranks (gloo) and the CPU oracle.
+"""
+import torch
+
+BLK = 64
+
+
+def chunk_bounds(n_total, world, align=BLK):
+    """Contiguous [lo, hi) per rank; interior boundaries are multiples of `align`."""
+    nb = -(-n_total // align)
+    cuts = [0] + [min(n_total, (nb * r // world) * align) for r in range(1, world)] + [n_total]
+    return [(cuts[r], cuts[r + 1]) for r in range(world)]
+
+
+def local_window(lo, hi, n_total, sink, local):
+    """Chunk-local [mask_lo, mask_hi): the tokens of [lo, hi) outside the global sink and local windows."""
+    n = hi - lo
+    mask_lo = min(max(sink - lo, 0), n)
+    mask_hi = min(max(n_total - local - lo, 0), n)
+    return mask_lo, max(mask_hi, mask_lo)
+
+
+def fixed_indices(n_total, sink, local, device=None):
+    return torch.cat([torch.arange(sink, device=device), torch.arange(n_total - local, n_total, device=device)])
+
+
+def all_gather(t, group=None):
+    """[W, *t.shape] of every rank's t (NCCL: one all_gather_into_tensor; gloo: list all_gather)."""
+    import torch.distributed as dist
+    W = dist.get_world_size(group)
+    if dist.get_backend(group) == "nccl":
+        out = torch.empty((W, *t.shape), dtype=t.dtype, device=t.device)
+        dist.all_gather_into_tensor(out, t.contiguous(), group=group)
+        return out
+    parts = [torch.empty_like(t) for _ in range(W)]
+    dist.all_gather(parts, t.contiguous(), group=group)
+    return torch.stack(parts)
+
+
+def sharded_select(scores, kk, lo, hi, n_total, sink, local, select_fn=None, merge_fn=None, gather_fn=None):
+    """Global top-kk indices [BH, G, kk] (int64, global) of a context-sharded score row set.
+
+    scores [BH, G, hi-lo] are this rank's chunk.  select_fn(scores, kk, mask_lo, mask_hi, offset) ->
+    (idx, vals); merge_fn(vals [..., m], idx [..., m], kk) -> idx; gather_fn(t) -> [W, *t.shape]."""
+    if select_fn is None:
+        from .bitplane import select_topk
+        select_fn = lambda s, k, a, b, off: select_topk(s, k, mask_lo=a, mask_hi=b, index_offset=off,
+                                                        with_scores=True)
+    if merge_fn is None:
+        from .bitplane import merge_topk
+        merge_fn = lambda v, i, k: merge_topk(v, i, k)[0]
+    gather_fn = gather_fn or all_gather
+    mlo, mhi = local_window(lo, hi, n_total, sink, local)
+    idx, vals = select_fn(scores, kk, mlo, mhi, lo)
+    BH, G, _ = idx.shape
+    packed = torch.stack([vals.float().view(torch.int32), idx.to(torch.int32)])      # one collective
+    allp = gather_fn(packed)                                                        # [W, 2, BH, G, kk]
+    W = allp.shape[0]
+    cv = allp[:, 0].view(torch.float32).permute(1, 2, 0, 3).reshape(BH, G, W * kk)
+    ci = allp[:, 1].to(torch.int64).permute(1, 2, 0, 3).reshape(BH, G, W * kk)
+    return merge_fn(cv, ci, kk)
+
+
+def sharded_decode_step(a, layers, kv, scores, outs, rank, world, q_in=None, g_in=None, scan_events=None):
+    """One decode step over all layers on a context-sharded index (see the module docstring).
+    `layers[L].store` holds this rank's chunk of a.ctx tokens; the context has a.ctx * world tokens."""
+    from . import bitplane as bp
+    from . import offload as off
+    n_total = a.ctx * world
+    lo, hi = rank * a.ctx, (rank + 1) * a.ctx
+    for L, lay in enumerate(layers):
+        q = lay.q if q_in is None else q_in[L]
+        g = lay.g if g_in is None else g_in[L]
+        plan = bp.make_plan(g, a.budget)
+        if scan_events is not None:
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+        s = lay.store.scan(q, plan, out=scores)
+        if scan_events is not None:
+            e1.record()
+            scan_events.append((e0, e1, lay.bytes))
+        top = sharded_select(s, a.k, lo, hi, n_total, a.sink, a.local)
+        BH, G, _ = top.shape
+        fixed = fixed_indices(n_total, a.sink, a.local, top.device).expand(BH, G, -1)
+        idx = torch.cat([top, fixed], -1)
+        kb, vb = kv[L % len(kv)]
+        part = off.decode_attention_partial(q, idx, kb.dev, vb.dev, a.ctx, lo, hi)
+        outs[L] = off.attention_combine(all_gather(part))
+    return outs

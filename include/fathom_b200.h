@@ -150,6 +150,25 @@ int fathom_decode_attention(const float* q, int64_t BH, int G, const int64_t* id
                             const uint16_t* V_recent, int64_t recent_cap, float* out_f32, uint16_t* out_bf16,
                             void* workspace, size_t workspace_bytes, void* stream);
 
+/* Workspace bytes of fathom_decode_attention_partial. */
+size_t fathom_decode_partial_workspace_bytes(int64_t BH, int G, int64_t k);
+
+/* Partial decode attention of one context shard.  Only picks in [idx_lo, idx_hi) are owned by this
+ * shard; they read row idx-idx_lo of K_src/V_src [BH][cap][128] (cap >= idx_hi-idx_lo).  Writes,
+ * per (bh, g), out_packed [BH][G][130] fp32 = (sum_r e^(s_r - m) V_r [128], m, l) with
+ * m = max owned score (-inf if none) and l = sum_r e^(s_r - m).  No reference counterpart (the
+ * reference runs on one GPU); it splits the attention of offload_attn
+ * (scripts/B_e2e_offload_v2.py:242-244) across context shards. */
+int fathom_decode_attention_partial(const float* q, int64_t BH, int G, const int64_t* idx, int64_t k,
+                                    const uint16_t* K_src, const uint16_t* V_src, int64_t cap, int64_t idx_lo,
+                                    int64_t idx_hi, float* out_packed, void* workspace, size_t workspace_bytes,
+                                    void* stream);
+
+/* Log-sum-exp merge of P shards' packed partials [P][rows][130] -> out [rows][128] (fp32 and/or
+ * bf16): out = sum_p o_p e^(m_p - M) / sum_p l_p e^(m_p - M), M = max_p m_p. */
+int fathom_attention_combine(const float* parts, int64_t P, int64_t rows, float* out_f32, uint16_t* out_bf16,
+                             void* stream);
+
 /* ---------------------------------------------------------------- host memory */
 
 /* Pinned, portable, mapped host allocation and its device alias (host_mapped,
