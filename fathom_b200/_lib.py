@@ -38,6 +38,7 @@ SIGNATURES = {
     "fathom_select_workspace_bytes": (SZ, [I64, I64, I64]),
     "fathom_select_topk": (I32, [P, I64, I64, I64, I64, I64, I64, I64, P, I64, P, P, SZ, P]),
     "fathom_sink_local_topk": (I32, [P, I64, I64, I64, I64, I64, P, P, SZ, P]),
+    "fathom_sink_local_topk_static": (I32, [P, I64, I64, I64, I64, I64, P, P]),
     "fathom_merge_topk": (I32, [P, P, I64, I64, I64, P, P, P]),
     "fathom_gather_rows": (I32, [P, I64, P, I64, I64, I64, P, P]),
     "fathom_decode_workspace_bytes": (SZ, [I64, I32, I64]),

@@ -18,6 +18,8 @@
 //               the keys equal to the threshold.
 #include "common.cuh"
 
+#include <atomic>
+
 namespace fathom {
 namespace {
 
@@ -379,4 +381,62 @@ extern "C" int fathom_merge_topk(const float* cand_scores, const int64_t* cand_i
   merge_kernel<<<(unsigned)rows, FT, smem, reinterpret_cast<cudaStream_t>(stream)>>>(cand_scores, cand_idx, m, kk,
                                                                                      out_idx, out_scores);
   return check_launch("merge_topk");
+}
+
+// ---------------------------------------------------------------------------------------------
+// Top-k with a library-owned scratch area: for callers that cannot allocate device memory on the
+// call path (a plugin host that has handed all device memory to its own pool, or a decode loop
+// that cannot accept cudaMalloc's implicit device synchronisation), and so cannot provide the
+// workspace fathom_sink_local_topk asks for.  The scratch is one file-scope device array sized for
+// FATHOM_STATIC_TOPK_MAX_ROWS rows; every GPU that loads this library holds it until the process
+// exits.  Every call on a device shares it: calls whose GPU work overlaps (other streams, other
+// host threads) race on it and must be serialised by the caller.  Each call clears the part that
+// has to start at zero (histograms and counters); the rest is overwritten before it is read.
+namespace fathom {
+namespace {
+
+constexpr size_t static_align256(size_t x) { return (x + 255) & ~(size_t)255; }
+constexpr size_t kStaticScratchBytes =
+    static_align256((size_t)FATHOM_STATIC_TOPK_MAX_ROWS * NBINS * sizeof(uint32_t)) +
+    static_align256((size_t)FATHOM_STATIC_TOPK_MAX_ROWS * sizeof(uint32_t)) +
+    static_align256((size_t)FATHOM_STATIC_TOPK_MAX_ROWS * CAP * sizeof(uint64_t));
+
+static __device__ __align__(256) unsigned char g_topk_scratch[kStaticScratchBytes];
+
+constexpr int kMaxDevices = 64;
+std::atomic<void*> g_topk_scratch_ptr[kMaxDevices];
+
+// Device address of g_topk_scratch on the current device.  In host code the array's name is only a
+// host-side stand-in, so the address is looked up once per device (with that device current) and
+// cached; the first call on each device therefore does this set-up.
+int static_scratch(void** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return set_error(FATHOM_ERR_CUDA, "sink_local_topk_static: cudaGetDevice: %s", cudaGetErrorString(e));
+  if (dev < 0 || dev >= kMaxDevices) return set_error(FATHOM_ERR_UNSUPPORTED, "sink_local_topk_static: device %d", dev);
+  void* p = g_topk_scratch_ptr[dev].load(std::memory_order_acquire);
+  if (p == nullptr) {
+    e = cudaGetSymbolAddress(&p, g_topk_scratch);
+    if (e != cudaSuccess || p == nullptr)
+      return set_error(FATHOM_ERR_CUDA, "sink_local_topk_static: cudaGetSymbolAddress: %s", cudaGetErrorString(e));
+    g_topk_scratch_ptr[dev].store(p, std::memory_order_release);
+  }
+  *out = p;
+  return FATHOM_OK;
+}
+
+}  // namespace
+}  // namespace fathom
+
+extern "C" int fathom_sink_local_topk_static(const float* scores, int64_t rows, int64_t n, int64_t k, int64_t sink,
+                                             int64_t local, int64_t* idx, void* stream) {
+  FATHOM_REQUIRE(rows >= 1 && rows <= FATHOM_STATIC_TOPK_MAX_ROWS, FATHOM_ERR_SHAPE,
+                 "sink_local_topk_static: rows=%lld outside 1..%d (the library-owned scratch holds at most %d rows; "
+                 "use fathom_sink_local_topk with a caller workspace for more)",
+                 (long long)rows, FATHOM_STATIC_TOPK_MAX_ROWS, FATHOM_STATIC_TOPK_MAX_ROWS);
+  FATHOM_REQUIRE(ws_bytes(rows) <= kStaticScratchBytes, FATHOM_ERR_WORKSPACE, "sink_local_topk_static: scratch too small");
+  void* scratch = nullptr;
+  const int r = static_scratch(&scratch);
+  if (r != FATHOM_OK) return r;
+  return fathom_sink_local_topk(scores, rows, n, k, sink, local, idx, scratch, kStaticScratchBytes, stream);
 }

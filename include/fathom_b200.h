@@ -118,6 +118,22 @@ int fathom_select_topk(const float* scores, int64_t rows, int64_t n, int64_t row
 int fathom_sink_local_topk(const float* scores, int64_t rows, int64_t n, int64_t k, int64_t sink, int64_t local,
                            int64_t* idx, void* workspace, size_t workspace_bytes, void* stream);
 
+/* Rows the library-owned scratch of fathom_sink_local_topk_static holds. */
+#define FATHOM_STATIC_TOPK_MAX_ROWS 64
+
+/* sink_local_topk exactly as fathom_sink_local_topk, but with no workspace argument and no
+ * allocation of any kind: for callers that cannot allocate device memory on the call path (a host
+ * whose device memory is all handed to its own pool, or a decode loop that cannot take
+ * cudaMalloc's implicit device synchronisation).  No counterpart in the reference.
+ * Scratch: one library-owned device array of about 5.3 MB, sized for FATHOM_STATIC_TOPK_MAX_ROWS
+ * rows, held by every GPU that loads the library until the process exits.  rows above that limit
+ * are rejected with FATHOM_ERR_SHAPE.  The first call on a device looks up the array's device
+ * address (cudaGetSymbolAddress) with that device current; make that first call before any
+ * stream capture.  All calls on a device share the array: calls whose GPU work overlaps
+ * (different streams or threads) race on it, so serialise them. */
+int fathom_sink_local_topk_static(const float* scores, int64_t rows, int64_t n, int64_t k, int64_t sink,
+                                  int64_t local, int64_t* idx, void* stream);
+
 /* Final top-kk of candidate lists [rows][m] (scores, global int64 indices < 2^32) in the
  * (score descending, index ascending) order: the merge of per-shard candidates of a
  * context-sharded scan.  No reference counterpart (the reference runs on one GPU);
