@@ -12,9 +12,11 @@ depends on the previous layer's output in a real model).
   value   scanned key-rows/s = T * Hkv * layers / step time, inputs (q, g) already on the device
   e2e     the same through the public API with host buffers: every step copies that step's
           queries and gains from pinned host memory and reads the attention outputs back
-  roofline  the scan kernel: algorithmic bytes (bytes_planes of each layer's plan) / its mean
-          CUDA-event duration, against the host link bandwidth measured in this run (pinned
-          H2D cudaMemcpy, 1 GiB)
+  roofline  the scan kernel (with the selection histogram in its epilogue): algorithmic bytes
+          (bytes_planes of each layer's plan) / its mean CUDA-event duration (events recorded on the
+          launching stream around the kernel: before the call's memset, and by the library right
+          after the kernel), against the host link bandwidth measured in this run (pinned H2D
+          cudaMemcpy, 1 GiB)
   hbm_resident  config 1 (T = 131072, index + K/V in HBM) as a secondary figure, against
           MEASURED_PEAKS.json hbm_gbs
   cpu_baseline  the CPU oracle (numpy restatement of the reference path) on a bounded sample
@@ -50,6 +52,8 @@ def parse():
     ap.add_argument("--ctx", type=int, default=1048576, help="tokens per rank")
     ap.add_argument("--layers", type=int, default=36)
     ap.add_argument("--kv-buffers", type=int, default=4, help="distinct host K/V row buffers, cycled over layers")
+    ap.add_argument("--kv-layout", choices=["interleaved", "separate"], default="interleaved",
+                    help="host K/V rows: one [BH][T][2][128] cache (K and V of a token adjacent) or two buffers")
     ap.add_argument("--hkv", type=int, default=8)
     ap.add_argument("--g", type=int, default=4)
     ap.add_argument("--budget", type=float, default=48.0)
@@ -143,13 +147,51 @@ class Layer:
     pass
 
 
+def host_budget(a):
+    """How many distinct index layers and K/V row buffers this rank can pin: everything the local ranks
+    pin must stay under 75% of the host's available memory (the rest is cycled over the layers)."""
+    avail = 0
+    try:
+        for line in open("/proc/meminfo"):
+            if line.startswith("MemAvailable:"):
+                avail = int(line.split()[1]) * 1024
+    except OSError:
+        pass
+    local = int(os.environ.get("LOCAL_WORLD_SIZE", "1"))
+    nblk = -(-a.ctx // 64)
+    per_index = a.hkv * 128 * nblk * (4 * 8 + 2)          # planes + scales of one layer
+    per_kv = 2 * a.hkv * a.ctx * 128 * 2                   # K and V rows of one layer
+    budget = 0.75 * avail / local if avail else float("inf")
+    n_kv = max(1, min(a.kv_buffers, a.layers))
+    n_index = a.layers
+    while n_index * per_index + n_kv * per_kv > budget and n_kv > 1:
+        n_kv -= 1
+    while n_index * per_index + n_kv * per_kv > budget and n_index > 1:
+        n_index -= 1
+    return n_index, n_kv
+
+
 def build_host_layers(a, dev, rank, world, bp, off):
     """Per layer: a host-order store of this rank's context chunk in mapped host memory, the layer's
-    query and gain on the device; K/V row buffers for the first kv_buffers layers."""
-    from fathom_b200.synth import make_layer
+    query and gain on the device; K/V row buffers for the first kv_buffers layers.  If the host cannot
+    pin a distinct index for every layer, later layers reuse the first indexes (same bytes moved)."""
     layers, kv = [], []
     BH = a.hkv
+    n_index, a.kv_buffers = host_budget(a)
+    a.index_buffers = n_index
     for L in range(a.layers):
+        if L >= n_index:                     # host memory exhausted: reuse an index (queries still differ)
+            src = layers[L % n_index]
+            lay = Layer()
+            qgen = torch.Generator(device=dev).manual_seed(777 + L)
+            scale = torch.randn(BH, 1, 128, generator=qgen, device=dev).exp()
+            lay.q = (torch.randn(BH, a.g, 128, generator=qgen, device=dev) * scale).contiguous()
+            lay.g = ((lay.q ** 2) * (scale[:, 0, None, :] ** 2)).sum(1).contiguous()
+            lay.store = src.store
+            plan = bp.make_plan(lay.g, a.budget)
+            lay.bytes = bp.bytes_planes(plan["t"], a.ctx)
+            layers.append(lay)
+            continue
         gen = torch.Generator(device=dev).manual_seed(1000 * (rank + 1) + L)
         qgen = torch.Generator(device=dev).manual_seed(777 + L)     # same query on every rank
         scale = torch.randn(BH, 1, 128, generator=qgen, device=dev).exp()
@@ -164,11 +206,17 @@ def build_host_layers(a, dev, rank, world, bp, off):
         lay.nact = float(plan["nact"].float().mean())
         if L < a.kv_buffers:
             V = (torch.randn(BH, a.ctx, 128, generator=gen, device=dev) * scale).to(torch.bfloat16)
-            kb = off.MappedBuffer(K.shape, torch.bfloat16, dev)
-            vb = off.MappedBuffer(V.shape, torch.bfloat16, dev)
-            kb.dev.copy_(K)
-            vb.dev.copy_(V)
-            kv.append((kb, vb))
+            if a.kv_layout == "interleaved":
+                buf = off.MappedBuffer((BH, a.ctx, 2, 128), torch.bfloat16, dev)
+                buf.dev[:, :, 0].copy_(K)
+                buf.dev[:, :, 1].copy_(V)
+                kv.append({"K": buf.dev[:, :, 0], "V": buf.dev[:, :, 1], "bufs": [buf]})
+            else:
+                kb = off.MappedBuffer(K.shape, torch.bfloat16, dev)
+                vb = off.MappedBuffer(V.shape, torch.bfloat16, dev)
+                kb.dev.copy_(K)
+                vb.dev.copy_(V)
+                kv.append({"K": kb.dev, "V": vb.dev, "bufs": [kb, vb]})
             del V
         del K
         torch.cuda.synchronize(dev)
@@ -185,14 +233,14 @@ def decode_step_1gpu(a, layers, kv, bp, off, scores, outs, q_in=None, g_in=None,
         plan = bp.make_plan(g, a.budget)
         if scan_events is not None:
             e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e1.record()    # creates the handle; the library records it again right after the scan kernel
             e0.record()
-        s = lay.store.scan(q, plan, out=scores)
+        idx = bp.scan_topk(lay.store, q, plan, k_tot, a.sink, a.local, scores=scores,
+                           scan_done_event=e1 if scan_events is not None else None)
         if scan_events is not None:
-            e1.record()
             scan_events.append((e0, e1, lay.bytes))
-        idx = bp.sink_local_topk(s, k_tot, a.sink, a.local)
-        kb, vb = kv[L % len(kv)]
-        outs[L] = off.decode_attention(q, idx, kb.dev, vb.dev, a.ctx)
+        rows = kv[L % len(kv)]
+        outs[L] = off.decode_attention(q, idx, rows["K"], rows["V"], a.ctx)
     return outs
 
 
@@ -251,7 +299,8 @@ def config_dict(a, world):
     return {"workload": "config2: host-resident index + K/V rows, Qwen3-8B attention shape, decode step",
             "ctx_per_gpu": a.ctx, "ctx_total": a.ctx * world, "layers": a.layers, "kv_heads": a.hkv,
             "q_per_kv": a.g, "head_dim": 128, "batch": 1, "budget": a.budget, "k": a.k, "sink": a.sink,
-            "local": a.local, "kv_row_buffers": a.kv_buffers,
+            "local": a.local, "kv_row_buffers": a.kv_buffers, "kv_layout": a.kv_layout,
+            "index_buffers": getattr(a, "index_buffers", a.layers),
             "parallelism": "context-shard" + str(world) if world > 1 else "single",
             "l2": "inputs larger than L2 (host index per step >> 126 MB)"}
 
@@ -277,12 +326,12 @@ def hbm_figure(a, dev, bp, off, peaks):
             plan = bp.make_plan(lay.g, a.budget)
             if ev is not None:
                 e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e1.record()    # creates the handle; the library records it again right after the scan kernel
                 e0.record()
-            s = lay.store.scan(lay.q, plan, out=scores)
+            idx = bp.scan_topk(lay.store, lay.q, plan, k_tot, a.sink, a.local, scores=scores,
+                               scan_done_event=e1 if ev is not None else None)
             if ev is not None:
-                e1.record()
                 ev.append((e0, e1, lay.bytes))
-            idx = bp.sink_local_topk(s, k_tot, a.sink, a.local)
             off.decode_attention(lay.q, idx, kvs[L][0], kvs[L][1], n)
 
     for _ in range(a.warmup):
@@ -300,19 +349,30 @@ def hbm_figure(a, dev, bp, off, peaks):
     e1.record()
     torch.cuda.synchronize()
     ms = e0.elapsed_time(e1) / a.steps
-    ev = []
-    for _ in range(2):
-        step(ev)
+    # the scan kernel alone, back to back in a graph (launch gaps removed): mean duration per layer
+    plans = [bp.make_plan(lay.g, a.budget) for lay in layers]
+    gs = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(gs):
+        for lay, plan in zip(layers, plans):
+            lay.store.scan(lay.q, plan, out=scores)
+    for _ in range(3):
+        gs.replay()
     torch.cuda.synchronize()
-    durs = [x.elapsed_time(y) for x, y, _ in ev]
-    byts = [b for _, _, b in ev]
-    scan_ms = float(np.mean(durs))
+    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    f0.record()
+    for _ in range(a.steps):
+        gs.replay()
+    f1.record()
+    torch.cuda.synchronize()
+    scan_ms = f0.elapsed_time(f1) / (a.steps * len(layers))
+    byts = [lay.bytes for lay in layers]
     achieved = float(np.mean(byts)) / (scan_ms * 1e-3) / 1e9
+    del gs
     rows = n * a.hkv * a.layers
     del g
     return {"workload": "config1: HBM-resident index + K/V, T=131072, 36 layers, graph-captured step",
             "value": rows / (ms * 1e-3), "unit": "key-rows/s", "ms_per_step": ms,
-            "scan_ms_per_layer": scan_ms,
+            "scan_ms_per_layer": scan_ms, "scan_timing": "36 scan launches in one CUDA graph, mean per launch",
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
                          "frac": achieved / peaks["hbm_gbs"], "traffic": None,
                          "bytes_per_launch": float(np.mean(byts))},
@@ -404,7 +464,8 @@ def main():
     scan_ms = float(np.mean(durs))
     achieved = float(np.mean(byts)) / (scan_ms * 1e-3) / 1e9
     bits_row = float(np.mean(byts)) * 8 / (a.ctx * a.hkv)
-    launches_per_layer = 7 if world == 1 else 8
+    # plan, scan (+ selection histogram), collect, finalize, dedupe, gather, attend; sharded: + merge, combine
+    launches_per_layer = 7 if world == 1 else 9
     line = {"metric": METRIC, "value": rows_step / (ms * 1e-3), "unit": "key-rows/s", "n_gpus": world,
             "steps": a.steps, "warmup": a.warmup, "ms_per_step": ms, "decode_step_us": ms * 1e3,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",

@@ -18,6 +18,8 @@ FATHOM_ERR_UNSUPPORTED = -3
 FATHOM_ERR_CUDA = -4
 FATHOM_ERR_WORKSPACE = -5
 
+HOST_HUGEPAGES = 1
+
 DTYPE_CODE = {torch.float32: 0, torch.bfloat16: 1, torch.float16: 2}
 
 P = ctypes.c_void_p
@@ -35,6 +37,9 @@ SIGNATURES = {
     "fathom_relayout": (I32, [P, P, I64, I64, I64, P, P, I64, P]),
     "fathom_make_plan": (I32, [P, P, I64, I32, I32, P, P, P, P, P, P, P, P]),
     "fathom_scan": (I32, [P, I64, I32, I64, I64, P, P, I32, P, P, I64, I64, P, P]),
+    "fathom_scan_select_workspace_bytes": (SZ, [I64, I32, I64, I64]),
+    "fathom_scan_select": (I32, [P, I64, I32, I64, I64, P, P, I32, P, P, I64, I64, I64, I64, I64, I64, P, P, I64, P,
+                                 P, SZ, P, P]),
     "fathom_select_workspace_bytes": (SZ, [I64, I64, I64]),
     "fathom_select_topk": (I32, [P, I64, I64, I64, I64, I64, I64, I64, P, I64, P, P, SZ, P]),
     "fathom_sink_local_topk": (I32, [P, I64, I64, I64, I64, I64, P, P, SZ, P]),
@@ -42,11 +47,12 @@ SIGNATURES = {
     "fathom_merge_topk": (I32, [P, P, I64, I64, I64, P, P, P]),
     "fathom_gather_rows": (I32, [P, I64, P, I64, I64, I64, P, P]),
     "fathom_decode_workspace_bytes": (SZ, [I64, I32, I64]),
-    "fathom_decode_attention": (I32, [P, I64, I32, P, I64, P, P, I64, I64, P, P, I64, P, P, P, SZ, P]),
+    "fathom_decode_attention": (I32, [P, I64, I32, P, I64, P, P, I64, I64, I64, P, P, I64, P, P, P, SZ, P]),
     "fathom_decode_partial_workspace_bytes": (SZ, [I64, I32, I64]),
-    "fathom_decode_attention_partial": (I32, [P, I64, I32, P, I64, P, P, I64, I64, I64, P, P, SZ, P]),
+    "fathom_decode_attention_partial": (I32, [P, I64, I32, P, I64, P, P, I64, I64, I64, I64, P, P, SZ, P]),
     "fathom_attention_combine": (I32, [P, I64, I64, P, P, P]),
     "fathom_host_alloc_mapped": (I32, [SZ, ctypes.POINTER(P), ctypes.POINTER(P)]),
+    "fathom_host_alloc_mapped_ex": (I32, [SZ, I32, ctypes.POINTER(P), ctypes.POINTER(P)]),
     "fathom_host_free": (I32, [P]),
 }
 

@@ -273,3 +273,40 @@ def merge_topk(cand_scores, cand_idx, kk):
     vals = torch.empty(rows, kk, dtype=torch.float32, device=dev)
     check(lib().fathom_merge_topk(ptr(cs), ptr(ci), rows, m, kk, ptr(idx), ptr(vals), stream_of(dev)), "merge_topk")
     return idx.view(*lead, kk), vals.view(*lead, kk)
+
+
+# ------------------------------------------------------------------ fused scan + selection
+def scan_select(store, q, plan, kk, mask_lo=0, mask_hi=None, index_offset=0, append_sink=0, append_local=0,
+                scores=None, with_scores=False, scan_done_event=None):
+    """store.scan(q, plan) and the top-kk selection of its rows in one fused pass (the selection
+    histogram is built in the scan epilogue).  Returns (idx int64 [BH, G, kk+append_sink+append_local],
+    vals fp32 [BH, G, kk] or None, scores fp32 [BH, G, n]).  scan_done_event (torch.cuda.Event) is
+    recorded right after the scan kernel."""
+    require_cuda(q)
+    BH, G, d = q.shape
+    assert BH == store.BH
+    dev = q.device
+    n = store.n
+    mask_hi = n if mask_hi is None else mask_hi
+    scores = torch.empty(BH, G, n, device=dev, dtype=torch.float32) if scores is None else scores
+    width = kk + append_sink + append_local
+    idx = torch.empty(BH, G, width, device=dev, dtype=torch.int64)
+    vals = torch.empty(BH, G, kk, device=dev, dtype=torch.float32) if with_scores else None
+    ws = _lib.workspace(dev, lib().fathom_scan_select_workspace_bytes(BH, G, n, kk), "select")
+    sub = getattr(store, "sub", None) or SUB
+    qc = q.contiguous().float()
+    cls, clsn = plan["cls"], plan["clsn"]
+    check(lib().fathom_scan_select(ptr(qc), BH, G, n, sub, ptr(cls), ptr(clsn), cls.shape[1], ptr(store.planes32),
+                                   ptr(store.scales_k), kk, mask_lo, mask_hi, index_offset, append_sink, append_local,
+                                   ptr(scores), ptr(idx), width, ptr(vals), ptr(ws), ws.numel(),
+                                   scan_done_event.cuda_event if scan_done_event is not None else None,
+                                   stream_of(dev)),
+          "scan_select")
+    return idx, vals, scores
+
+
+def scan_topk(store, q, plan, k, sink=4, local=32, scores=None, scan_done_event=None):
+    """sink_local_topk(store.scan(q, plan), k, sink, local) in one fused pass; int64 [BH, G, k]."""
+    idx, _, _ = scan_select(store, q, plan, k - sink - local, mask_lo=sink, mask_hi=store.n - local,
+                            append_sink=sink, append_local=local, scores=scores, scan_done_event=scan_done_event)
+    return idx

@@ -2,34 +2,43 @@
 // (scripts/B_e2e_offload_v2.py:73-83 gather_rows, :226-244 offload_attn tail;
 //  HBM twin scripts/B_kernel_bench.py:26-31 gather_attn).
 //
-// decode attention, two launches:
-//   1 dedupe_gather  one CTA per (batch, kv-head): bitonic sort of the G*k selected indices,
-//                    unique ranks by a block scan, slot map (query head, pick) -> unique row, and
-//                    a gather of each unique K and V row ONCE from its source (mapped host memory
-//                    or the device-resident recent buffer) into a device staging area; 16 B per
-//                    lane, 16 lanes per 256-byte row, several rows in flight per thread.
-//   2 attend         one CTA per (batch, query head): q.K^T / sqrt(128) over its k picks from the
-//                    staging area, max-subtracted softmax and the weighted sum of V, fp32 math.
+// decode attention, three launches:
+//   1 dedupe   one CTA per (batch, kv-head): the G*k picks go into a shared-memory hash table,
+//              a block scan ranks the distinct indices; slot map (query head, pick) -> unique row,
+//              the unique index list (in table order) and its length.
+//   2 gather   many CTAs per (batch, kv-head): each unique K and V row is fetched ONCE from its source
+//              (mapped host memory over the host link, or the device-resident recent buffer) into a
+//              device staging area; 16 lanes x 16 B per 256-byte row, 4 rows in flight per lane.
+//              Spreading the rows over every SM keeps enough requests in flight for the link.
+//   3 attend   one CTA of 32 warps per (batch, query head): each warp takes 4 picks at a time from
+//              the staging area (L2-resident), q.K^T / sqrt(128), an online softmax and the running
+//              weighted sum of V; the 16 warp states are merged in shared memory.  fp32 math.
+// A pick outside the caller's owned index range [idx_lo, idx_hi) is skipped (context shards);
+// the partial form writes the unnormalised output with its (max, sum of exp).
 #include "common.cuh"
 
 namespace fathom {
 namespace {
 
-constexpr int DT = 1024;    // dedupe_gather threads
-constexpr int AT = 256;     // attend threads
-constexpr int MAX_M = 16384;  // G*k per (batch, kv-head) handled by one CTA
+constexpr int DT = 1024;      // dedupe threads
+constexpr int GT = 256;       // gather threads
+constexpr int GROWS = 64;     // unique rows per gather CTA
+constexpr int AW = 32;        // attend warps
+constexpr int AU = 4;         // picks per warp iteration
+constexpr int MAX_M = 16384;  // G*k per (batch, kv-head) handled by one dedupe CTA
 
 size_t align256(size_t x) { return (x + 255) & ~(size_t)255; }
 
 struct DecodeWs {
-  int32_t* slot;       // [BH][M]
-  int64_t* uniq;       // [BH][M] unique indices of each row, ascending
+  int32_t* slot;       // [BH][M] pick -> unique row (-1: not owned)
+  int64_t* uniq;       // [BH][M] unique indices, ascending (-1: not owned)
+  int32_t* ucount;     // [BH] number of unique indices
   uint16_t* kstage;    // [BH][M][128] bf16
   uint16_t* vstage;    // [BH][M][128] bf16
 };
 
 size_t decode_ws_bytes(int64_t BH, int64_t M) {
-  return align256(BH * M * sizeof(int32_t)) + align256(BH * M * sizeof(int64_t)) +
+  return align256(BH * M * sizeof(int32_t)) + align256(BH * M * sizeof(int64_t)) + align256(BH * sizeof(int32_t)) +
          2 * align256(BH * M * D * sizeof(uint16_t));
 }
 
@@ -40,29 +49,12 @@ DecodeWs carve(void* base, int64_t BH, int64_t M) {
   p += align256(BH * M * sizeof(int32_t));
   w.uniq = reinterpret_cast<int64_t*>(p);
   p += align256(BH * M * sizeof(int64_t));
+  w.ucount = reinterpret_cast<int32_t*>(p);
+  p += align256(BH * sizeof(int32_t));
   w.kstage = reinterpret_cast<uint16_t*>(p);
   p += align256(BH * M * D * sizeof(uint16_t));
   w.vstage = reinterpret_cast<uint16_t*>(p);
   return w;
-}
-
-__device__ void bitonic_asc(uint64_t* s, int P) {
-  for (int k = 2; k <= P; k <<= 1) {
-    for (int j = k >> 1; j > 0; j >>= 1) {
-      for (int i = threadIdx.x; i < P; i += blockDim.x) {
-        const int ixj = i ^ j;
-        if (ixj > i) {
-          const uint64_t a = s[i], b = s[ixj];
-          const bool asc = (i & k) == 0;
-          if (asc ? (a > b) : (a < b)) {
-            s[i] = b;
-            s[ixj] = a;
-          }
-        }
-      }
-      __syncthreads();
-    }
-  }
 }
 
 __device__ uint32_t block_exclusive_scan(uint32_t v, uint32_t* s_warp, uint32_t* total) {
@@ -93,85 +85,118 @@ __device__ uint32_t block_exclusive_scan(uint32_t v, uint32_t* s_warp, uint32_t*
   return res;
 }
 
-constexpr int POS_BITS = 24;  // position of a pick within G*k (< 2^24); index in the upper 40 bits
+constexpr uint32_t EMPTY = 0xFFFFFFFFu;
+constexpr int MAX_TS = 32768;         // hash table slots (128 KB of shared memory)
+constexpr int PICKS_PER_THREAD = MAX_M / DT;
 
-__global__ void __launch_bounds__(DT) dedupe_gather_kernel(const int64_t* __restrict__ idx, int64_t M,
-                                                           int64_t idx_lo, int64_t idx_hi,
-                                                           const uint4* __restrict__ ksrc, const uint4* __restrict__ vsrc,
-                                                           int64_t cap, int64_t n_host, const uint4* __restrict__ krec,
-                                                           const uint4* __restrict__ vrec, int64_t recent_cap,
-                                                           int32_t* __restrict__ slot, int64_t* __restrict__ uniq,
-                                                           uint4* __restrict__ kstage,
-                                                           uint4* __restrict__ vstage) {
-  extern __shared__ uint64_t s_sort[];  // P entries
+__device__ __forceinline__ uint32_t hash_slot(uint32_t key, int log2ts) {
+  return (key * 0x9E3779B1u) >> (32 - log2ts);
+}
+
+// One CTA per (batch, kv-head).  Every owned pick is inserted into an open-addressing table in
+// shared memory (atomicCAS, linear probing; the table has at least twice as many slots as picks,
+// so a probe sequence always ends at an empty slot or at its own key).  A block scan over the
+// table then ranks the distinct indices; each pick remembers its table slot and reads its rank.
+__global__ void __launch_bounds__(DT) dedupe_kernel(const int64_t* __restrict__ idx, int64_t M, int64_t idx_lo,
+                                                    int64_t idx_hi, int64_t row_limit, int log2ts,
+                                                    int32_t* __restrict__ slot,
+                                                    int64_t* __restrict__ uniq, int32_t* __restrict__ ucount) {
+  extern __shared__ uint32_t s_tab[];  // 1 << log2ts slots
   __shared__ uint32_t s_warp[33];
   const int64_t bh = blockIdx.x;
-  int P = 1;
-  while (P < M) P <<= 1;
-  const int64_t* ib = idx + bh * M;
-  for (int i = threadIdx.x; i < P; i += blockDim.x)
-    s_sort[i] = i < M ? ((uint64_t)ib[i] << POS_BITS) | (uint64_t)i : ~0ull;
+  const int TS = 1 << log2ts;
+  for (int i = threadIdx.x; i < TS; i += blockDim.x) s_tab[i] = EMPTY;
   __syncthreads();
-  bitonic_asc(s_sort, P);
-
-  // slot map (pick position -> unique rank) and the unique index list, from the sorted picks
-  int32_t* sl = slot + bh * M;
-  int64_t* ul = uniq + bh * M;
-  uint32_t base = 0;
-  for (int64_t c0 = 0; c0 < M; c0 += blockDim.x) {
-    const int64_t i = c0 + threadIdx.x;
-    uint64_t v = 0;
-    bool first = false;
-    if (i < M) {
-      v = s_sort[i];
-      first = i == 0 || (v >> POS_BITS) != (s_sort[i - 1] >> POS_BITS);
-    }
-    uint32_t tot;
-    const uint32_t ex = block_exclusive_scan(first ? 1u : 0u, s_warp, &tot);
-    if (i < M) {
-      const int64_t t = (int64_t)(v >> POS_BITS);
-      const bool owned = t >= idx_lo && t < idx_hi;
-      sl[v & ((1ull << POS_BITS) - 1)] = owned ? (int32_t)(base + ex - (first ? 0u : 1u)) : -1;
-      if (first) ul[base + ex] = owned ? t - idx_lo : -1;
-    }
-    base += tot;
-  }
-  __syncthreads();  // makes the unique list (global) visible to the whole CTA
-  const int64_t U = base;
-  // gather: 16 lanes x 16 B per 256-byte row; K and V
-  constexpr int LPR = D * 2 / 16;  // uint4 per row = 16
-  const int sub = threadIdx.x % LPR;
-  const int rows_per_iter = blockDim.x / LPR;
-  uint4* ks = kstage + bh * M * LPR;
-  uint4* vs = vstage + bh * M * LPR;
-  constexpr int UNROLL = 4;
-  for (int64_t r0 = threadIdx.x / LPR; r0 < U; r0 += (int64_t)rows_per_iter * UNROLL) {
-    uint4 kv[UNROLL], vv[UNROLL];
+  const int64_t* ib = idx + bh * M;
+  int pos[PICKS_PER_THREAD];
 #pragma unroll
-    for (int u = 0; u < UNROLL; ++u) {
-      const int64_t r = r0 + (int64_t)u * rows_per_iter;
-      const int64_t t = r < U ? ul[r] : -1;
-      if (t >= 0) {
-        const uint4* kp;
-        const uint4* vp;
-        if (t < n_host) {
-          kp = ksrc + (bh * cap + t) * LPR;
-          vp = vsrc + (bh * cap + t) * LPR;
-        } else {
-          kp = krec + (bh * recent_cap + (t - n_host)) * LPR;
-          vp = vrec + (bh * recent_cap + (t - n_host)) * LPR;
+  for (int u = 0; u < PICKS_PER_THREAD; ++u) {
+    const int64_t i = threadIdx.x + (int64_t)u * DT;
+    pos[u] = -1;
+    if (i < M) {
+      const int64_t t = ib[i];
+      if (t >= idx_lo && t < idx_hi && t - idx_lo < row_limit) {
+        const uint32_t key = (uint32_t)(t - idx_lo);
+        uint32_t h = hash_slot(key, log2ts);
+        for (int probe = 0; probe < TS; ++probe) {
+          const uint32_t old = atomicCAS(&s_tab[h], EMPTY, key);
+          if (old == EMPTY || old == key) {
+            pos[u] = (int)h;
+            break;
+          }
+          h = (h + 1) & (TS - 1);
         }
-        kv[u] = kp[sub];
-        vv[u] = vp[sub];
       }
     }
+  }
+  __syncthreads();
+  // rank the occupied slots (each thread a contiguous chunk of the table)
+  const int per = TS / DT > 0 ? TS / DT : 1;
+  const int h0 = threadIdx.x * per;
+  uint32_t cnt = 0;
+  for (int h = h0; h < h0 + per && h < TS; ++h) cnt += s_tab[h] != EMPTY;
+  uint32_t total;
+  uint32_t r = block_exclusive_scan(cnt, s_warp, &total);
+  int64_t* ul = uniq + bh * M;
+  for (int h = h0; h < h0 + per && h < TS; ++h) {
+    const uint32_t key = s_tab[h];
+    if (key != EMPTY) {
+      ul[r] = (int64_t)key;
+      s_tab[h] = r++;     // the slot now holds the rank (keys are no longer needed)
+    }
+  }
+  __syncthreads();
+  int32_t* sl = slot + bh * M;
 #pragma unroll
-    for (int u = 0; u < UNROLL; ++u) {
-      const int64_t r = r0 + (int64_t)u * rows_per_iter;
-      if (r < U && ul[r] >= 0) {
-        ks[r * LPR + sub] = kv[u];
-        vs[r * LPR + sub] = vv[u];
+  for (int u = 0; u < PICKS_PER_THREAD; ++u) {
+    const int64_t i = threadIdx.x + (int64_t)u * DT;
+    if (i < M) sl[i] = pos[u] >= 0 ? (int32_t)s_tab[pos[u]] : -1;
+  }
+  if (threadIdx.x == 0) ucount[bh] = (int32_t)total;
+}
+
+__global__ void __launch_bounds__(GT) gather_kernel(const int32_t* __restrict__ ucount, const int64_t* __restrict__ uniq,
+                                                    int64_t M, const uint4* __restrict__ ksrc,
+                                                    const uint4* __restrict__ vsrc, int64_t cap, int64_t rs16,
+                                                    int64_t n_host,
+                                                    const uint4* __restrict__ krec, const uint4* __restrict__ vrec,
+                                                    int64_t recent_cap, uint4* __restrict__ kstage,
+                                                    uint4* __restrict__ vstage) {
+  constexpr int LPR = D * 2 / 16;          // 16 lanes x 16 B per row
+  constexpr int RPP = GT / LPR;            // rows per pass
+  constexpr int PASSES = GROWS / RPP;      // 4
+  const int64_t bh = blockIdx.y;
+  const int64_t U = ucount[bh];
+  const int64_t r0 = (int64_t)blockIdx.x * GROWS;
+  if (r0 >= U) return;
+  const int sub = threadIdx.x % LPR;
+  const int rr = threadIdx.x / LPR;
+  uint4 kv[PASSES], vv[PASSES];
+  int64_t rows[PASSES];
+#pragma unroll
+  for (int u = 0; u < PASSES; ++u) {
+    const int64_t r = r0 + u * RPP + rr;
+    const int64_t t = r < U ? uniq[bh * M + r] : -1;
+    rows[u] = t >= 0 ? r : -1;
+    if (t >= 0) {
+      const uint4* kp;
+      const uint4* vp;
+      if (t < n_host) {  // host rows: rs16 uint4 between consecutive rows (LPR when K and V are separate)
+        kp = ksrc + (bh * cap + t) * rs16;
+        vp = vsrc + (bh * cap + t) * rs16;
+      } else {
+        kp = krec + (bh * recent_cap + (t - n_host)) * LPR;
+        vp = vrec + (bh * recent_cap + (t - n_host)) * LPR;
       }
+      kv[u] = kp[sub];
+      vv[u] = vp[sub];
+    }
+  }
+#pragma unroll
+  for (int u = 0; u < PASSES; ++u) {
+    if (rows[u] >= 0) {
+      kstage[(bh * M + rows[u]) * LPR + sub] = kv[u];
+      vstage[(bh * M + rows[u]) * LPR + sub] = vv[u];
     }
   }
 }
@@ -179,79 +204,95 @@ __global__ void __launch_bounds__(DT) dedupe_gather_kernel(const int64_t* __rest
 __device__ __forceinline__ float bf16lo(uint32_t w) { return __uint_as_float(w << 16); }
 __device__ __forceinline__ float bf16hi(uint32_t w) { return __uint_as_float(w & 0xffff0000u); }
 
-__global__ void __launch_bounds__(AT) attend_kernel(const float* __restrict__ q, int G, int64_t k, int64_t M,
-                                                    const int32_t* __restrict__ slot, const uint16_t* __restrict__ kstage,
-                                                    const uint16_t* __restrict__ vstage, float* __restrict__ out_f32,
-                                                    uint16_t* __restrict__ out_bf16, float* __restrict__ out_ml) {
-  extern __shared__ float s_p[];  // k probabilities
-  __shared__ float s_q[D];
-  __shared__ float s_red[AT / 32];
-  __shared__ float s_acc[2][D];
+// out_packed != NULL: partial form, [BH*G][130] = (sum_r e^(s_r - m) V_r, m, l).
+__global__ void __launch_bounds__(AW * 32) attend_kernel(const float* __restrict__ q, int G, int64_t k, int64_t M,
+                                                         const int32_t* __restrict__ slot,
+                                                         const uint16_t* __restrict__ kstage,
+                                                         const uint16_t* __restrict__ vstage,
+                                                         float* __restrict__ out_f32, uint16_t* __restrict__ out_bf16,
+                                                         float* __restrict__ out_packed) {
+  __shared__ float s_m[AW], s_l[AW];
+  __shared__ float s_acc[AW][D];
   const int64_t bhg = blockIdx.x;
   const int64_t bh = bhg / G, g = bhg % G;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  if (tid < D) s_q[tid] = q[bhg * D + tid];
-  __syncthreads();
+  const float4 qv = *reinterpret_cast<const float4*>(q + bhg * D + lane * 4);
   const int32_t* sl = slot + bh * M + g * k;
-  const uint16_t* kb = kstage + bh * M * D;
-  const uint16_t* vb = vstage + bh * M * D;
+  const uint16_t* kb = kstage + bh * M * D + lane * 4;
+  const uint16_t* vb = vstage + bh * M * D + lane * 4;
   const float scale = rsqrtf((float)D);
-  // scores: one warp per pick, 4 dims per lane
-  float qv[4];
+  float m = -INFINITY, l = 0.0f, a0 = 0.0f, a1 = 0.0f, a2 = 0.0f, a3 = 0.0f;
+  for (int64_t r0 = (int64_t)warp * AU; r0 < k; r0 += (int64_t)AW * AU) {
+    int32_t sr[AU];
+    uint2 kw[AU], vw[AU];
 #pragma unroll
-  for (int i = 0; i < 4; ++i) qv[i] = s_q[lane * 4 + i];
-  float mloc = -INFINITY;
-  for (int64_t r = warp; r < k; r += AT / 32) {
-    const int32_t sr = sl[r];
-    float d = -INFINITY;
-    if (sr >= 0) {  // slot -1: the pick is owned by another context shard
-      const uint2 w = *reinterpret_cast<const uint2*>(kb + (int64_t)sr * D + lane * 4);
-      d = qv[0] * bf16lo(w.x) + qv[1] * bf16hi(w.x) + qv[2] * bf16lo(w.y) + qv[3] * bf16hi(w.y);
-      d = warp_sum(d) * scale;
+    for (int u = 0; u < AU; ++u) {
+      sr[u] = r0 + u < k ? sl[r0 + u] : -1;
+      kw[u] = sr[u] >= 0 ? *reinterpret_cast<const uint2*>(kb + (int64_t)sr[u] * D) : make_uint2(0, 0);
+      vw[u] = sr[u] >= 0 ? *reinterpret_cast<const uint2*>(vb + (int64_t)sr[u] * D) : make_uint2(0, 0);
     }
-    if (lane == 0) s_p[r] = d;
-    mloc = fmaxf(mloc, d);
-  }
-  if (lane == 0) s_red[warp] = mloc;
-  __syncthreads();
-  float m = -INFINITY;
+    float sc[AU];
 #pragma unroll
-  for (int i = 0; i < AT / 32; ++i) m = fmaxf(m, s_red[i]);
-  __syncthreads();
-  float sloc = 0.0f;
-  for (int64_t r = tid; r < k; r += AT) {
-    const float e = s_p[r] == -INFINITY ? 0.0f : expf(s_p[r] - m);
-    s_p[r] = e;
-    sloc += e;
-  }
-  sloc = warp_sum(sloc);
-  if (lane == 0) s_red[warp] = sloc;
-  __syncthreads();
-  float ssum = 0.0f;
+    for (int u = 0; u < AU; ++u)
+      sc[u] = qv.x * bf16lo(kw[u].x) + qv.y * bf16hi(kw[u].x) + qv.z * bf16lo(kw[u].y) + qv.w * bf16hi(kw[u].y);
 #pragma unroll
-  for (int i = 0; i < AT / 32; ++i) ssum += s_red[i];
-  // weighted V: thread -> (dimension, parity of the pick)
-  const int dim = tid & (D - 1), par = tid >> 7;
-  float acc = 0.0f;
-  for (int64_t r = par; r < k; r += 2) {
-    const int32_t sr = sl[r];
-    if (sr >= 0) {
-      const uint16_t v = vb[(int64_t)sr * D + dim];
-      acc = fmaf(s_p[r], __uint_as_float((uint32_t)v << 16), acc);
+    for (int o = 16; o > 0; o >>= 1) {
+#pragma unroll
+      for (int u = 0; u < AU; ++u) sc[u] += __shfl_xor_sync(0xffffffffu, sc[u], o);
     }
+    float mx = m;
+#pragma unroll
+    for (int u = 0; u < AU; ++u) {
+      sc[u] = sr[u] >= 0 ? sc[u] * scale : -INFINITY;
+      mx = fmaxf(mx, sc[u]);
+    }
+    if (mx == -INFINITY) continue;  // nothing owned yet
+    const float corr = m == -INFINITY ? 0.0f : expf(m - mx);
+    l *= corr;
+    a0 *= corr;
+    a1 *= corr;
+    a2 *= corr;
+    a3 *= corr;
+#pragma unroll
+    for (int u = 0; u < AU; ++u) {
+      const float p = sc[u] == -INFINITY ? 0.0f : expf(sc[u] - mx);
+      l += p;
+      a0 = fmaf(p, bf16lo(vw[u].x), a0);
+      a1 = fmaf(p, bf16hi(vw[u].x), a1);
+      a2 = fmaf(p, bf16lo(vw[u].y), a2);
+      a3 = fmaf(p, bf16hi(vw[u].y), a3);
+    }
+    m = mx;
   }
-  s_acc[par][dim] = acc;
+  if (lane == 0) {
+    s_m[warp] = m;
+    s_l[warp] = l;
+  }
+  s_acc[warp][lane * 4 + 0] = a0;
+  s_acc[warp][lane * 4 + 1] = a1;
+  s_acc[warp][lane * 4 + 2] = a2;
+  s_acc[warp][lane * 4 + 3] = a3;
   __syncthreads();
   if (tid < D) {
-    const float un = s_acc[0][tid] + s_acc[1][tid];
-    if (out_ml) {  // partial: unnormalised sum, with (max, sum of exp) beside it
-      out_f32[bhg * D + tid] = un;
+    float Mx = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < AW; ++w) Mx = fmaxf(Mx, s_m[w]);
+    float L = 0.0f, O = 0.0f;
+#pragma unroll
+    for (int w = 0; w < AW; ++w) {
+      const float e = s_m[w] == -INFINITY ? 0.0f : expf(s_m[w] - Mx);
+      L = fmaf(s_l[w], e, L);
+      O = fmaf(s_acc[w][tid], e, O);
+    }
+    if (out_packed) {
+      float* pk = out_packed + bhg * (D + 2);
+      pk[tid] = O;
       if (tid == 0) {
-        out_ml[bhg * 2] = m;
-        out_ml[bhg * 2 + 1] = ssum;
+        pk[D] = Mx;
+        pk[D + 1] = L;
       }
     } else {
-      const float o = un / ssum;
+      const float o = O / L;
       if (out_f32) out_f32[bhg * D + tid] = o;
       if (out_bf16) out_bf16[bhg * D + tid] = __bfloat16_as_ushort(__float2bfloat16_rn(o));
     }
@@ -280,14 +321,6 @@ __global__ void __launch_bounds__(D) combine_kernel(const float* __restrict__ pa
   if (out_bf16) out_bf16[row * D + t] = __bfloat16_as_ushort(__float2bfloat16_rn(o));
 }
 
-__global__ void pack_partial_kernel(const float* __restrict__ o, const float* __restrict__ ml, int64_t rows,
-                                    float* __restrict__ packed) {
-  const int64_t row = blockIdx.x;
-  const int t = threadIdx.x;
-  packed[row * (D + 2) + t] = o[row * D + t];
-  if (t < 2) packed[row * (D + 2) + D + t] = ml[row * 2 + t];
-}
-
 __global__ void gather_rows_kernel(const uint4* __restrict__ src, int64_t cap, const int32_t* __restrict__ idx,
                                    int64_t R, int lpr, uint4* __restrict__ dst) {
   const int64_t bh = blockIdx.y;
@@ -296,19 +329,20 @@ __global__ void gather_rows_kernel(const uint4* __restrict__ src, int64_t cap, c
   const int sub = threadIdx.x % lpr;
   if (r >= R || threadIdx.x >= rows_per_cta * lpr) return;
   const int32_t t = idx[bh * R + r];
-  if (t < 0) return;
+  if (t < 0 || t >= cap) return;  // skipped: no traffic (negative) or outside the source rows
   dst[(bh * R + r) * lpr + sub] = src[(bh * cap + t) * lpr + sub];
 }
 
 
 int run_decode(const float* q, int64_t BH, int G, const int64_t* idx, int64_t k, const uint16_t* K_src,
-               const uint16_t* V_src, int64_t cap, int64_t n_host, const uint16_t* K_recent, const uint16_t* V_recent,
+               const uint16_t* V_src, int64_t cap, int64_t kv_row_stride, int64_t n_host, const uint16_t* K_recent,
+               const uint16_t* V_recent,
                int64_t recent_cap, int64_t idx_lo, int64_t idx_hi, float* out_f32, uint16_t* out_bf16,
-               float* out_ml, void* workspace, size_t workspace_bytes, cudaStream_t st) {
+               float* out_packed, void* workspace, size_t workspace_bytes, cudaStream_t st) {
   FATHOM_REQUIRE(q && idx && K_src && V_src && workspace, FATHOM_ERR_NULL, "decode_attention: NULL pointer");
-  FATHOM_REQUIRE(out_f32 || out_bf16, FATHOM_ERR_NULL, "decode_attention: no output");
-  FATHOM_REQUIRE(BH >= 1 && G >= 1 && k >= 1 && n_host >= 0 && n_host <= cap && idx_lo <= idx_hi, FATHOM_ERR_SHAPE,
-                 "decode_attention: bad shape");
+  FATHOM_REQUIRE(out_f32 || out_bf16 || out_packed, FATHOM_ERR_NULL, "decode_attention: no output");
+  FATHOM_REQUIRE(BH >= 1 && BH <= 65535 && G >= 1 && k >= 1 && n_host >= 0 && n_host <= cap && idx_lo <= idx_hi,
+                 FATHOM_ERR_SHAPE, "decode_attention: bad shape");
   const int64_t M = (int64_t)G * k;
   FATHOM_REQUIRE(M <= MAX_M, FATHOM_ERR_UNSUPPORTED, "decode_attention: G*k=%lld exceeds %d", (long long)M, MAX_M);
   FATHOM_REQUIRE(recent_cap == 0 || (K_recent && V_recent), FATHOM_ERR_NULL,
@@ -316,22 +350,31 @@ int run_decode(const float* q, int64_t BH, int G, const int64_t* idx, int64_t k,
   FATHOM_REQUIRE(workspace_bytes >= decode_ws_bytes(BH, M) && (reinterpret_cast<uintptr_t>(workspace) & 255) == 0,
                  FATHOM_ERR_WORKSPACE, "decode_attention: workspace needs %zu bytes, 256-byte aligned",
                  decode_ws_bytes(BH, M));
-  FATHOM_REQUIRE((reinterpret_cast<uintptr_t>(K_src) & 15) == 0 && (reinterpret_cast<uintptr_t>(V_src) & 15) == 0,
-                 FATHOM_ERR_SHAPE, "decode_attention: K/V sources must be 16-byte aligned");
+  FATHOM_REQUIRE((reinterpret_cast<uintptr_t>(K_src) & 15) == 0 && (reinterpret_cast<uintptr_t>(V_src) & 15) == 0 &&
+                     (reinterpret_cast<uintptr_t>(q) & 15) == 0,
+                 FATHOM_ERR_SHAPE, "decode_attention: q and the K/V sources must be 16-byte aligned");
   DecodeWs w = carve(workspace, BH, M);
-  int P = 1;
-  while (P < M) P <<= 1;
-  const size_t smem = (size_t)P * sizeof(uint64_t);
-  cudaFuncSetAttribute(dedupe_gather_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  dedupe_gather_kernel<<<(unsigned)BH, DT, smem, st>>>(
-      idx, M, idx_lo, idx_hi, reinterpret_cast<const uint4*>(K_src), reinterpret_cast<const uint4*>(V_src), cap,
-      n_host, reinterpret_cast<const uint4*>(K_recent), reinterpret_cast<const uint4*>(V_recent), recent_cap, w.slot,
-      w.uniq, reinterpret_cast<uint4*>(w.kstage), reinterpret_cast<uint4*>(w.vstage));
-  const size_t smem2 = (size_t)k * sizeof(float);
-  FATHOM_REQUIRE(smem2 <= 160 * 1024, FATHOM_ERR_UNSUPPORTED, "decode_attention: k too large");
-  cudaFuncSetAttribute(attend_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem2);
-  attend_kernel<<<(unsigned)(BH * G), AT, smem2, st>>>(q, G, k, M, w.slot, w.kstage, w.vstage, out_f32, out_bf16,
-                                                       out_ml);
+  FATHOM_REQUIRE(cap < 0xFFFFFFFFLL && n_host + recent_cap < 0xFFFFFFFFLL, FATHOM_ERR_UNSUPPORTED,
+                 "decode_attention: row indices must fit 32 bits");
+  if (kv_row_stride == 0) kv_row_stride = D;
+  FATHOM_REQUIRE(kv_row_stride >= D && kv_row_stride % 8 == 0, FATHOM_ERR_SHAPE,
+                 "decode_attention: kv_row_stride must be >= 128 and a multiple of 8 elements");
+  int log2ts = 10;
+  while ((1 << log2ts) < 2 * M) ++log2ts;           // load factor <= 1/2
+  FATHOM_REQUIRE((1 << log2ts) <= MAX_TS, FATHOM_ERR_UNSUPPORTED, "decode_attention: too many picks");
+  const size_t smem = (size_t)sizeof(uint32_t) << log2ts;
+  cudaFuncSetAttribute(dedupe_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  // picks at or beyond the readable rows (n_host host rows + recent_cap device rows) are ignored
+  dedupe_kernel<<<(unsigned)BH, DT, smem, st>>>(idx, M, idx_lo, idx_hi, n_host + recent_cap, log2ts, w.slot, w.uniq,
+                                                w.ucount);
+  dim3 ggrid((unsigned)cdiv(M, GROWS), (unsigned)BH);
+  gather_kernel<<<ggrid, GT, 0, st>>>(w.ucount, w.uniq, M, reinterpret_cast<const uint4*>(K_src),
+                                      reinterpret_cast<const uint4*>(V_src), cap, kv_row_stride / 8, n_host,
+                                      reinterpret_cast<const uint4*>(K_recent),
+                                      reinterpret_cast<const uint4*>(V_recent), recent_cap,
+                                      reinterpret_cast<uint4*>(w.kstage), reinterpret_cast<uint4*>(w.vstage));
+  attend_kernel<<<(unsigned)(BH * G), AW * 32, 0, st>>>(q, G, k, M, w.slot, w.kstage, w.vstage, out_f32, out_bf16,
+                                                         out_packed);
   return check_launch("decode_attention");
 }
 
@@ -346,37 +389,30 @@ extern "C" size_t fathom_decode_workspace_bytes(int64_t BH, int G, int64_t k) {
 }
 
 extern "C" int fathom_decode_attention(const float* q, int64_t BH, int G, const int64_t* idx, int64_t k,
-                                       const uint16_t* K_src, const uint16_t* V_src, int64_t cap, int64_t n_host,
-                                       const uint16_t* K_recent, const uint16_t* V_recent, int64_t recent_cap,
-                                       float* out_f32, uint16_t* out_bf16, void* workspace, size_t workspace_bytes,
-                                       void* stream) {
-  return run_decode(q, BH, G, idx, k, K_src, V_src, cap, n_host, K_recent, V_recent, recent_cap, 0, INT64_MAX,
+                                       const uint16_t* K_src, const uint16_t* V_src, int64_t cap,
+                                       int64_t kv_row_stride, int64_t n_host, const uint16_t* K_recent,
+                                       const uint16_t* V_recent, int64_t recent_cap, float* out_f32,
+                                       uint16_t* out_bf16, void* workspace, size_t workspace_bytes, void* stream) {
+  return run_decode(q, BH, G, idx, k, K_src, V_src, cap, kv_row_stride, n_host, K_recent, V_recent, recent_cap, 0,
+                    INT64_MAX,
                     out_f32, out_bf16, nullptr, workspace, workspace_bytes, reinterpret_cast<cudaStream_t>(stream));
 }
 
 extern "C" int fathom_decode_attention_partial(const float* q, int64_t BH, int G, const int64_t* idx, int64_t k,
                                                const uint16_t* K_src, const uint16_t* V_src, int64_t cap,
-                                               int64_t idx_lo, int64_t idx_hi, float* out_packed, void* workspace,
-                                               size_t workspace_bytes, void* stream) {
+                                               int64_t kv_row_stride, int64_t idx_lo, int64_t idx_hi,
+                                               float* out_packed, void* workspace, size_t workspace_bytes,
+                                               void* stream) {
   FATHOM_REQUIRE(out_packed, FATHOM_ERR_NULL, "decode_attention_partial: NULL output");
   FATHOM_REQUIRE(idx_hi - idx_lo <= cap, FATHOM_ERR_SHAPE, "decode_attention_partial: owned range exceeds cap");
-  const size_t need = decode_ws_bytes(BH, (int64_t)G * k);
-  const size_t extra = align256((size_t)BH * G * (D + 2) * sizeof(float));
-  FATHOM_REQUIRE(workspace_bytes >= need + extra, FATHOM_ERR_WORKSPACE,
-                 "decode_attention_partial: workspace needs %zu bytes", need + extra);
-  float* o = reinterpret_cast<float*>(static_cast<char*>(workspace) + need);
-  float* ml = o + (size_t)BH * G * D;
-  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-  int r = run_decode(q, BH, G, idx, k, K_src, V_src, cap, idx_hi - idx_lo, nullptr, nullptr, 0, idx_lo, idx_hi, o,
-                     nullptr, ml, workspace, need, st);
-  if (r != FATHOM_OK) return r;
-  pack_partial_kernel<<<(unsigned)(BH * G), D, 0, st>>>(o, ml, BH * G, out_packed);
-  return check_launch("decode_attention_partial");
+  return run_decode(q, BH, G, idx, k, K_src, V_src, cap, kv_row_stride, idx_hi - idx_lo, nullptr, nullptr, 0, idx_lo,
+                    idx_hi, nullptr,
+                    nullptr, out_packed, workspace, workspace_bytes, reinterpret_cast<cudaStream_t>(stream));
 }
 
 extern "C" size_t fathom_decode_partial_workspace_bytes(int64_t BH, int G, int64_t k) {
   if (BH <= 0 || G <= 0 || k <= 0) return 0;
-  return decode_ws_bytes(BH, (int64_t)G * k) + align256((size_t)BH * G * (D + 2) * sizeof(float));
+  return decode_ws_bytes(BH, (int64_t)G * k);
 }
 
 extern "C" int fathom_attention_combine(const float* parts, int64_t P, int64_t rows, float* out_f32, uint16_t* out_bf16,

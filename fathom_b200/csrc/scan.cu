@@ -11,95 +11,148 @@
 // so each (token, channel) costs t shift+or pairs and one FMA per query head.
 //
 // Work split: a warp owns a group of consecutive 64-token blocks of one (batch, kv-head) row;
-// each lane owns TPL tokens of one 32-bit plane half-word (TPL = 32: 16 blocks per warp, TPL = 16:
-// 8 blocks per warp, used for G > 4 to bound registers).  For a (channel, plane) a warp's loads
-// are consecutive 4-byte words, i.e. fully coalesced 128-byte (or 64-byte) segments in both the
-// HBM order (sub = 16) and the host run order (sub = nblk).  Every lane keeps G x TPL fp32
-// accumulators in registers; the query tile and the channel lists sit in shared memory.  The
-// next channel's plane words are loaded before the current channel is consumed.
-#include "common.cuh"
+// each lane owns TPL tokens of one 32-bit plane half-word: TPL = 32 (16 blocks per warp), 16 (8
+// blocks) or 8 (4 blocks).  The launch picks the largest TPL that still gives every SM enough
+// warps (small problems such as 128k tokens x 8 heads need the finer split; G > 4 never uses 32,
+// to bound registers).  For a (channel, plane) the warp's words are 128 (64, 32) consecutive
+// bytes in both the HBM order (sub = 16) and the host run order (sub = nblk).  Every lane keeps
+// G x TPL fp32 accumulators in registers; the query tile and the channel list sit in shared memory.
+//
+// Memory parallelism: the channel list is cut into batches of about WB plane words.  One lane per
+// half-word copies the words (and the 4-byte word holding the block scale) of the next batch into
+// shared memory with cp.async while the warp computes the current batch from the other buffer, so
+// a warp keeps a whole batch in flight instead of one channel.  Lanes sharing a half-word read the
+// copy after cp.async.wait_group and a warp barrier; a second warp barrier guards buffer reuse.
+#include "select_common.cuh"
+
+#include <stdlib.h>
 
 namespace fathom {
 namespace {
 
 constexpr int WARPS = 4;
+constexpr int WB = 32;            // a batch holds the channels whose first word slot falls in [b*WB, (b+1)*WB)
+constexpr int WBUF = WB + 3;      // ... so its words span at most WB + 3 slots
+constexpr int CB = WB;            // and at most WB channels (each has >= 1 word)
+template <int TPL>
+constexpr int stage_u32() { return (WBUF + CB) * (32 * TPL / 32); }  // one buffer of one warp: (WBUF+CB) x half-words
+constexpr int MAXB = D * NPLANES / WB + 2;   // batch boundaries
+
+__device__ __forceinline__ void cp_async4(uint32_t* smem_dst, const void* gsrc) {
+  const uint32_t d = static_cast<uint32_t>(__cvta_generic_to_shared(smem_dst));
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;\n" ::"r"(d), "l"(gsrc) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory");
+}
 
 template <int G, int TPL, int C>
-__device__ __forceinline__ void scan_class(float (&acc)[G][TPL], float (&cst)[G], const float (*s_q)[D],
-                                           const int* s_ch, int i0, int i1, const uint32_t* __restrict__ pbase,
-                                           const uint16_t* __restrict__ sbase, int64_t chan_stride32,
-                                           int64_t plane_stride32, int64_t sub, int bitoff, bool active) {
-  if (i0 >= i1) return;
-  constexpr float KC = (C == 1 ? 0.5f : C == 2 ? 0.25f : C == 3 ? 0.125f : 0.0625f) - 3.0f;
-  uint32_t wn[C];
-  uint16_t sn = 0;
-  {
-    const int ch = s_ch[i0];
+__device__ __forceinline__ void tokens(float (&acc)[G][TPL], const uint32_t (&w)[4], const float (&W)[G]) {
 #pragma unroll
-    for (int p = 0; p < C; ++p) wn[p] = active ? __ldg(pbase + ch * chan_stride32 + p * plane_stride32) : 0u;
-    sn = active ? __ldg(sbase + ch * sub) : (uint16_t)0;
-  }
-  for (int i = i0; i < i1; ++i) {
-    const int ch = s_ch[i];
-    uint32_t w[C];
+  for (int k = 0; k < TPL; ++k) {
+    uint32_t bits = 0x3F800000u;
 #pragma unroll
-    for (int p = 0; p < C; ++p) w[p] = wn[p] >> bitoff;
-    const float sc = __half2float(__ushort_as_half(sn));
-    if (i + 1 < i1) {
-      const int chn = s_ch[i + 1];
-#pragma unroll
-      for (int p = 0; p < C; ++p) wn[p] = active ? __ldg(pbase + chn * chan_stride32 + p * plane_stride32) : 0u;
-      sn = active ? __ldg(sbase + chn * sub) : (uint16_t)0;
+    for (int p = 0; p < C; ++p) {
+      const int sh = 22 - p - k;
+      const uint32_t m = sh >= 0 ? (w[p] << sh) : (w[p] >> (-sh));
+      bits |= m & (1u << (22 - p));
     }
-    float W[G];
+    const float f = __uint_as_float(bits);
 #pragma unroll
-    for (int g = 0; g < G; ++g) {
-      const float qs = s_q[g][ch] * sc;
-      W[g] = 2.0f * qs;
-      cst[g] = fmaf(qs, KC, cst[g]);
-    }
-#pragma unroll
-    for (int k = 0; k < TPL; ++k) {
-      uint32_t bits = 0x3F800000u;
-#pragma unroll
-      for (int p = 0; p < C; ++p) {
-        const int sh = 22 - p - k;
-        const uint32_t m = sh >= 0 ? (w[p] << sh) : (w[p] >> (-sh));
-        bits |= m & (1u << (22 - p));
-      }
-      const float f = __uint_as_float(bits);
-#pragma unroll
-      for (int g = 0; g < G; ++g) acc[g][k] = fmaf(W[g], f, acc[g][k]);
-    }
+    for (int g = 0; g < G; ++g) acc[g][k] = fmaf(W[g], f, acc[g][k]);
   }
 }
 
-template <int G, int TPL>
-__global__ void __launch_bounds__(WARPS * 32, 2)
+// Selection histogram fused into the scan epilogue (HIST = true): the same 4096-bin histogram of the
+// top 12 key bits that the selection's hist pass builds, for tokens in [mask_lo, mask_hi).
+struct HistArgs {
+  int64_t mask_lo, mask_hi, kk;
+  uint32_t* hist;    // [BH*G][4096]
+  uint32_t* ticket;  // [BH] CTAs finished per (batch, kv-head) row
+  uint32_t* bstar;   // [BH*G] boundary bins
+};
+
+template <int TPL, int G>
+constexpr int min_blocks() { return TPL == 32 ? 2 : TPL == 16 ? (G > 4 ? 2 : 3) : (G > 4 ? 3 : 5); }
+
+template <int G, int TPL, bool HIST>
+__global__ void __launch_bounds__(WARPS * 32, (min_blocks<TPL, G>()))
     scan_kernel(const float* __restrict__ q, const int32_t* __restrict__ cls, const int32_t* __restrict__ clsn,
                 int bmax, const uint32_t* __restrict__ planes32, const uint16_t* __restrict__ scales, int64_t n,
                 int64_t nblk, int64_t nsb, int64_t sub, int64_t blk_begin, int64_t blk_end, int64_t grp_begin,
-                float* __restrict__ out) {
-  constexpr int BPW = TPL == 32 ? 16 : 8;  // blocks per warp
+                float* __restrict__ out, HistArgs ha) {
+  constexpr int LPW = 32 / TPL;          // lanes sharing a plane half-word
+  constexpr int NHW = 32 / LPW;          // half-words per warp
+  constexpr int BPW = NHW / 2;           // blocks per warp
+  constexpr int STAGE_U32 = stage_u32<TPL>();
+  extern __shared__ uint32_t s_stage[];  // [WARPS][2][STAGE_U32], then (HIST) [G][NBINS/2] packed u16 counters
   __shared__ float s_q[G][D];
-  __shared__ int s_ch[D];
-  __shared__ int s_start[NPLANES + 1];
+  __shared__ int s_ch[D], s_t[D], s_slot[D];
+  __shared__ int s_bstart[MAXB + 1];
+  __shared__ int s_nb;
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int64_t bh = blockIdx.y;
+  uint32_t* s_hist = s_stage + WARPS * 2 * STAGE_U32;
+  if (HIST)
+    for (int e = tid; e < G * selectk::NBINS / 2; e += blockDim.x) s_hist[e] = 0;
   for (int e = tid; e < G * D; e += blockDim.x) s_q[e / D][e % D] = q[bh * G * D + e];
-  if (tid == 0) {
-    int s = 0;
-    for (int c = 1; c <= NPLANES; ++c) {
-      s_start[c - 1] = s;
-      s += c <= bmax ? clsn[bh * bmax + c - 1] : 0;
-    }
-    s_start[NPLANES] = s;
+  // one round of global loads: the query tile above, and here every thread's column of the four
+  // class lists plus the class counts; then the flat channel list in class order (depth 1, 2, 3, 4).
+  // Entry i of class c sits at flat index cstart[c] + i and word slot cword[c] + c * i; its batch
+  // is slot / WB.
+  int cnt4[NPLANES];
+  int ch4[NPLANES];
+#pragma unroll
+  for (int c = 0; c < NPLANES; ++c) {
+    int v = c < bmax ? clsn[bh * bmax + c] : 0;
+    cnt4[c] = v < 0 ? 0 : (v > D ? D : v);             // memory safety for foreign plans
+    ch4[c] = (c < bmax && tid < D) ? cls[(bh * bmax + c) * D + tid] : 0;
   }
-  __syncthreads();
-  for (int c = 1; c <= bmax; ++c) {
-    const int cnt = s_start[c] - s_start[c - 1];
-    for (int i = tid; i < cnt; i += blockDim.x) s_ch[s_start[c - 1] + i] = cls[(bh * bmax + c - 1) * D + i];
+  int cstart[NPLANES + 1], cword[NPLANES];
+  {
+    int st = 0, wd = 0;
+#pragma unroll
+    for (int c = 0; c < NPLANES; ++c) {
+      cstart[c] = st;
+      cword[c] = wd;
+      st += cnt4[c];
+      wd += (c + 1) * cnt4[c];
+    }
+    cstart[NPLANES] = st;
+  }
+  const int total = cstart[NPLANES];
+  if (tid == 0) s_nb = 0;
+  __syncthreads();   // s_nb reset before any thread closes the last batch below
+#pragma unroll
+  for (int c = 0; c < NPLANES; ++c) {
+    const int i = tid;
+    if (i < cnt4[c]) {
+      const int m = cstart[c] + i;
+      const int t = c + 1;
+      const int slot = cword[c] + t * i;
+      s_ch[m] = ch4[c] & (D - 1);                      // channel ids are 0..127
+      s_t[m] = t;
+      const int b = slot / WB;
+      s_slot[m] = slot - b * WB;
+      // the previous flat entry's batch (entry i-1 of this class, or the last of an earlier class)
+      int prev = -1;
+      if (m > 0) {
+        int pc = c, pi = i - 1;
+        while (pi < 0) {
+          --pc;
+          pi = cnt4[pc] - 1;
+        }
+        prev = (cword[pc] + (pc + 1) * pi) / WB;
+      }
+      if (b != prev) s_bstart[b] = m;
+      if (m == total - 1) {  // the last channel closes the last batch
+        s_nb = b + 1;
+        s_bstart[b + 1] = m + 1;
+      }
+    }
   }
   __syncthreads();
 
@@ -107,26 +160,38 @@ __global__ void __launch_bounds__(WARPS * 32, 2)
   const int64_t wblk0 = grp * BPW;
   const int64_t lo = blk_begin > wblk0 ? blk_begin : wblk0;
   const int64_t hi_lim = blk_end < nblk ? blk_end : nblk;
-  if (lo >= hi_lim || wblk0 + BPW <= blk_begin) return;  // whole warp outside the range
+  const bool warp_live = !(lo >= hi_lim || wblk0 + BPW <= blk_begin);  // some block of the warp in range
 
-  int64_t blk, half;
-  int bitoff;
-  if (TPL == 32) {
-    blk = wblk0 + (lane >> 1);
-    half = lane & 1;
-    bitoff = 0;
-  } else {
-    blk = wblk0 + (lane >> 2);
-    half = (lane >> 1) & 1;
-    bitoff = (lane & 1) * 16;
-  }
-  const bool active = blk >= blk_begin && blk < hi_lim;
+  const int hw = lane / LPW;                 // this lane's half-word within the warp
+  const int64_t blk = wblk0 + (hw >> 1);
+  const int64_t half = hw & 1;
+  const int bitoff = (lane % LPW) * TPL;
+  const bool issuer = (lane % LPW) == 0;
+  const bool active = warp_live && blk >= blk_begin && blk < hi_lim;
   const int64_t bsafe = active ? blk : lo;
   const int64_t sb = bsafe / sub, s_in = bsafe - sb * sub;
   const uint32_t* pbase = planes32 + ((bh * nsb + sb) * D * NPLANES * sub + s_in) * 2 + half;
-  const uint16_t* sbase = scales + (bh * nsb + sb) * D * sub + s_in;
   const int64_t plane_stride32 = sub * 2;
   const int64_t chan_stride32 = NPLANES * sub * 2;
+  const int64_t sc_elem0 = (bh * nsb + sb) * D * sub + s_in;   // scale element of channel 0
+
+  uint32_t* stage = s_stage + warp * 2 * STAGE_U32;
+  const int nbatch = warp_live ? s_nb : 0;
+
+  auto issue = [&](int b) {
+    uint32_t* wbuf = stage + (b & 1) * STAGE_U32;
+    uint32_t* sbuf = wbuf + WBUF * NHW;
+    if (active && issuer) {
+      for (int i = s_bstart[b]; i < s_bstart[b + 1]; ++i) {
+        const int ch = s_ch[i], t = s_t[i], slot = s_slot[i];
+        const uint32_t* gp = pbase + ch * chan_stride32;
+        for (int p = 0; p < t; ++p) cp_async4(&wbuf[(slot + p) * NHW + hw], gp + p * plane_stride32);
+        const int64_t e = sc_elem0 + (int64_t)ch * sub;            // the aligned 4-byte word holding it
+        cp_async4(&sbuf[(i - s_bstart[b]) * NHW + hw], scales + (e & ~(int64_t)1));
+      }
+    }
+    cp_async_commit();
+  };
 
   float acc[G][TPL];
   float cst[G];
@@ -136,46 +201,131 @@ __global__ void __launch_bounds__(WARPS * 32, 2)
 #pragma unroll
     for (int k = 0; k < TPL; ++k) acc[g][k] = 0.0f;
   }
-  scan_class<G, TPL, 1>(acc, cst, s_q, s_ch, s_start[0], s_start[1], pbase, sbase, chan_stride32, plane_stride32, sub,
-                        bitoff, active);
-  scan_class<G, TPL, 2>(acc, cst, s_q, s_ch, s_start[1], s_start[2], pbase, sbase, chan_stride32, plane_stride32, sub,
-                        bitoff, active);
-  scan_class<G, TPL, 3>(acc, cst, s_q, s_ch, s_start[2], s_start[3], pbase, sbase, chan_stride32, plane_stride32, sub,
-                        bitoff, active);
-  scan_class<G, TPL, 4>(acc, cst, s_q, s_ch, s_start[3], s_start[4], pbase, sbase, chan_stride32, plane_stride32, sub,
-                        bitoff, active);
-  if (!active) return;
 
-  const int64_t tok0 = blk * BLK + half * 32 + bitoff;
-  const bool full = tok0 + TPL <= n;
-  const bool vec = full && (n % 4 == 0) && ((reinterpret_cast<uintptr_t>(out) & 15) == 0);
-#pragma unroll
-  for (int g = 0; g < G; ++g) {
-    float* o = out + (bh * G + g) * n + tok0;
-    if (vec) {
-#pragma unroll
-      for (int k = 0; k < TPL; k += 4)
-        *reinterpret_cast<float4*>(o + k) =
-            make_float4(acc[g][k] + cst[g], acc[g][k + 1] + cst[g], acc[g][k + 2] + cst[g], acc[g][k + 3] + cst[g]);
+  if (nbatch > 0) issue(0);
+  for (int b = 0; b < nbatch; ++b) {
+    if (LPW > 1) __syncwarp();             // every lane is done with the buffer issue(b + 1) refills
+    if (b + 1 < nbatch) {
+      issue(b + 1);
+      cp_async_wait<1>();
     } else {
+      cp_async_wait<0>();
+    }
+    if (LPW > 1) __syncwarp();             // the issuers' copies are visible to the whole warp
+    const uint32_t* wbuf = stage + (b & 1) * STAGE_U32;
+    const uint32_t* sbuf = wbuf + WBUF * NHW;
+    for (int i = s_bstart[b]; i < s_bstart[b + 1]; ++i) {
+      const int ch = s_ch[i], t = s_t[i], slot = s_slot[i];
+      const int64_t e = sc_elem0 + (int64_t)ch * sub;
+      const uint32_t sw = sbuf[(i - s_bstart[b]) * NHW + hw];
+      const float sc = active ? __half2float(__ushort_as_half((uint16_t)(sw >> ((e & 1) * 16)))) : 0.0f;
+      uint32_t w[4];
 #pragma unroll
-      for (int k = 0; k < TPL; ++k)
-        if (tok0 + k < n) o[k] = acc[g][k] + cst[g];
+      for (int p = 0; p < 4; ++p) w[p] = (p < t && active) ? (wbuf[(slot + p) * NHW + hw] >> bitoff) : 0u;
+      float W[G];
+      const float KC = __uint_as_float(0x3F800000u - ((uint32_t)t << 23)) - 3.0f;   // 2^-t - 3
+#pragma unroll
+      for (int g = 0; g < G; ++g) {
+        const float qs = s_q[g][ch] * sc;
+        W[g] = 2.0f * qs;
+        cst[g] = fmaf(qs, KC, cst[g]);
+      }
+      switch (t) {
+        case 1: tokens<G, TPL, 1>(acc, w, W); break;
+        case 2: tokens<G, TPL, 2>(acc, w, W); break;
+        case 3: tokens<G, TPL, 3>(acc, w, W); break;
+        default: tokens<G, TPL, 4>(acc, w, W); break;
+      }
+    }
+  }
+  const int64_t tok0 = blk * BLK + half * 32 + bitoff;
+  if (active) {
+    const bool full = tok0 + TPL <= n;
+    const bool vec = full && (n % 4 == 0) && ((reinterpret_cast<uintptr_t>(out) & 15) == 0);
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+      float* o = out + (bh * G + g) * n + tok0;
+      if (vec) {
+#pragma unroll
+        for (int k = 0; k < TPL; k += 4)
+          *reinterpret_cast<float4*>(o + k) = make_float4(acc[g][k] + cst[g], acc[g][k + 1] + cst[g],
+                                                          acc[g][k + 2] + cst[g], acc[g][k + 3] + cst[g]);
+      } else {
+#pragma unroll
+        for (int k = 0; k < TPL; ++k)
+          if (tok0 + k < n) o[k] = acc[g][k] + cst[g];
+      }
+    }
+  }
+  if (HIST) {
+    if (active) {
+      // this lane's tokens, as a bit mask of the ones that are counted unmasked (the rest count as -inf)
+      const bool plain = tok0 >= ha.mask_lo && tok0 + TPL <= ha.mask_hi && tok0 + TPL <= n;
+#pragma unroll
+      for (int g = 0; g < G; ++g) {
+#pragma unroll
+        for (int k = 0; k < TPL; ++k) {
+          const int64_t tok = tok0 + k;
+          if (plain || tok < n) {
+            const bool in = plain || (tok >= ha.mask_lo && tok < ha.mask_hi);
+            const uint32_t key = in ? f2key(acc[g][k] + cst[g]) : KEY_NEG_INF;
+            const uint32_t bin = key >> (32 - selectk::HBITS);
+            atomicAdd(&s_hist[g * (selectk::NBINS / 2) + (bin >> 1)], 1u << ((bin & 1) * 16));
+          }
+        }
+      }
+    }
+    __syncthreads();
+    for (int e = tid; e < G * selectk::NBINS / 2; e += blockDim.x) {
+      const uint32_t v = s_hist[e];
+      if (v) {
+        const int g = e / (selectk::NBINS / 2), b2 = (e % (selectk::NBINS / 2)) * 2;
+        uint32_t* gh = ha.hist + (bh * G + g) * selectk::NBINS + b2;
+        if (v & 0xFFFFu) atomicAdd(gh, v & 0xFFFFu);
+        if (v >> 16) atomicAdd(gh + 1, v >> 16);
+      }
+    }
+    // the last CTA of this (batch, kv-head) row derives the G boundary bins (no CTA waits)
+    __shared__ bool s_last;
+    __shared__ uint32_t s_part[WARPS * 32];
+    __shared__ int s_res;
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) s_last = atomicAdd(&ha.ticket[bh], 1u) == gridDim.x - 1;
+    __syncthreads();
+    if (s_last) {
+      __threadfence();
+      uint32_t* s_row = s_stage;  // the staging buffers are free now
+      for (int g = 0; g < G; ++g) {
+        const uint32_t* gh = ha.hist + (bh * G + g) * selectk::NBINS;
+        for (int b = tid; b < selectk::NBINS; b += blockDim.x) s_row[b] = __ldcg(&gh[b]);
+        __syncthreads();
+        const int bs = selectk::boundary_bin(s_row, ha.kk, s_part, &s_res);
+        if (tid == 0) ha.bstar[bh * G + g] = (uint32_t)bs;
+        __syncthreads();
+      }
     }
   }
 }
 
-template <int G, int TPL>
+template <int G, int TPL, bool HIST>
 int launch_scan(const float* q, int64_t BH, int64_t n, int64_t nblk, int64_t nsb, int64_t sub, const int32_t* cls,
                 const int32_t* clsn, int bmax, const uint32_t* planes32, const uint16_t* scales, int64_t b0, int64_t b1,
-                float* out, cudaStream_t st) {
-  constexpr int BPW = TPL == 32 ? 16 : 8;
+                float* out, const HistArgs& ha, cudaStream_t st) {
+  constexpr int BPW = TPL / 2;
   const int64_t g0 = b0 / BPW, g1 = cdiv(b1, BPW);
   const int64_t grid_x = cdiv(g1 - g0, WARPS);
   FATHOM_REQUIRE(grid_x <= 0x7fffffffLL && BH <= 65535, FATHOM_ERR_SHAPE, "scan: grid too large");
+  size_t smem = (size_t)WARPS * 2 * stage_u32<TPL>() * sizeof(uint32_t);
+  if (HIST) {  // the histogram follows the staging area, and the last CTA reuses staging for one row
+    smem += (size_t)G * selectk::NBINS / 2 * sizeof(uint32_t);
+    const size_t row_bytes = selectk::NBINS * sizeof(uint32_t);
+    if (smem < row_bytes) smem = row_bytes;
+  }
+  cudaFuncSetAttribute(scan_kernel<G, TPL, HIST>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   dim3 grid((unsigned)grid_x, (unsigned)BH);
-  scan_kernel<G, TPL><<<grid, WARPS * 32, 0, st>>>(q, cls, clsn, bmax, planes32, scales, n, nblk, nsb, sub, b0, b1, g0,
-                                                   out);
+  scan_kernel<G, TPL, HIST><<<grid, WARPS * 32, smem, st>>>(q, cls, clsn, bmax, planes32, scales, n, nblk, nsb, sub,
+                                                            b0, b1, g0, out, ha);
   return check_launch("scan");
 }
 
@@ -184,34 +334,119 @@ int launch_scan(const float* q, int64_t BH, int64_t n, int64_t nblk, int64_t nsb
 
 using namespace fathom;
 
-extern "C" int fathom_scan(const float* q, int64_t BH, int G, int64_t n, int64_t sub, const int32_t* cls,
-                           const int32_t* clsn, int bmax, const uint64_t* planes_k, const uint16_t* scales_k,
-                           int64_t blk_begin, int64_t blk_end, float* scores, void* stream) {
+namespace fathom {
+namespace {
+int sm_count() {
+  static int cached[64] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+  if (cached[dev] == 0) {
+    int v = 0;
+    cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev);
+    cached[dev] = v > 0 ? v : 148;
+  }
+  return cached[dev];
+}
+
+int scan_dispatch(const float* q, int64_t BH, int G, int64_t n, int64_t sub, const int32_t* cls, const int32_t* clsn,
+                  int bmax, const uint64_t* planes_k, const uint16_t* scales_k, int64_t blk_begin, int64_t blk_end,
+                  float* scores, const HistArgs* ha, cudaStream_t st) {
   FATHOM_REQUIRE(q && cls && clsn && planes_k && scales_k && scores, FATHOM_ERR_NULL, "scan: NULL pointer");
   FATHOM_REQUIRE(BH >= 1 && BH <= 65535 && n >= 1 && sub >= 1, FATHOM_ERR_SHAPE, "scan: bad shape (BH=%lld n=%lld)",
                  (long long)BH, (long long)n);
   FATHOM_REQUIRE(G >= 1 && G <= 8, FATHOM_ERR_UNSUPPORTED, "scan: G must be in 1..8 (got %d)", G);
   FATHOM_REQUIRE(bmax >= 1 && bmax <= NPLANES, FATHOM_ERR_SHAPE, "scan: bmax must be in 1..4");
+  FATHOM_REQUIRE((reinterpret_cast<uintptr_t>(planes_k) & 7) == 0 && (reinterpret_cast<uintptr_t>(scales_k) & 3) == 0,
+                 FATHOM_ERR_SHAPE, "scan: planes must be 8-byte and scales 4-byte aligned");
   const int64_t nblk = cdiv(n, BLK), nsb = cdiv(nblk, sub);
   FATHOM_REQUIRE(blk_begin >= 0 && blk_begin <= blk_end && blk_end <= nblk, FATHOM_ERR_SHAPE,
                  "scan: block range [%lld, %lld) outside [0, %lld]", (long long)blk_begin, (long long)blk_end,
                  (long long)nblk);
   if (blk_begin == blk_end) return FATHOM_OK;
-  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   const uint32_t* p32 = reinterpret_cast<const uint32_t*>(planes_k);
-#define FATHOM_SCAN_CASE(GG, TT) \
-  case GG:                       \
-    return launch_scan<GG, TT>(q, BH, n, nblk, nsb, sub, cls, clsn, bmax, p32, scales_k, blk_begin, blk_end, scores, st);
-  switch (G) {
-    FATHOM_SCAN_CASE(1, 32)
-    FATHOM_SCAN_CASE(2, 32)
-    FATHOM_SCAN_CASE(3, 32)
-    FATHOM_SCAN_CASE(4, 32)
-    FATHOM_SCAN_CASE(5, 16)
-    FATHOM_SCAN_CASE(6, 16)
-    FATHOM_SCAN_CASE(7, 16)
-    FATHOM_SCAN_CASE(8, 16)
+  HistArgs none{};
+  // tokens per lane: 32 for G <= 4 (16 for G > 4, to bound registers); a split 4x finer only when the
+  // coarse one would leave most SMs without a warp
+  const int64_t range = blk_end - blk_begin;
+  auto warps_for = [&](int tpl) { return BH * cdiv(range, tpl / 2); };
+  int tpl = G <= 4 ? 32 : 16;
+  if (warps_for(tpl) < (int64_t)sm_count()) tpl = 8;
+  if (const char* env = getenv("FATHOM_SCAN_TPL")) {  // tuning override: 8, 16 or 32
+    const int v = atoi(env);
+    if (v == 8 || v == 16 || (v == 32 && G <= 4)) tpl = v;
   }
-#undef FATHOM_SCAN_CASE
+#define FATHOM_SCAN_LAUNCH(GG, TT)                                                                                  \
+  return ha ? launch_scan<GG, TT, true>(q, BH, n, nblk, nsb, sub, cls, clsn, bmax, p32, scales_k, blk_begin,        \
+                                        blk_end, scores, *ha, st)                                                   \
+            : launch_scan<GG, TT, false>(q, BH, n, nblk, nsb, sub, cls, clsn, bmax, p32, scales_k, blk_begin,       \
+                                         blk_end, scores, none, st);
+#define FATHOM_SCAN_CASE4(GG)                    \
+  case GG:                                       \
+    if (tpl == 32) { FATHOM_SCAN_LAUNCH(GG, 32) } \
+    if (tpl == 16) { FATHOM_SCAN_LAUNCH(GG, 16) } \
+    FATHOM_SCAN_LAUNCH(GG, 8)
+#define FATHOM_SCAN_CASE8(GG)                    \
+  case GG:                                       \
+    if (tpl == 16) { FATHOM_SCAN_LAUNCH(GG, 16) } \
+    FATHOM_SCAN_LAUNCH(GG, 8)
+  switch (G) {
+    FATHOM_SCAN_CASE4(1)
+    FATHOM_SCAN_CASE4(2)
+    FATHOM_SCAN_CASE4(3)
+    FATHOM_SCAN_CASE4(4)
+    FATHOM_SCAN_CASE8(5)
+    FATHOM_SCAN_CASE8(6)
+    FATHOM_SCAN_CASE8(7)
+    FATHOM_SCAN_CASE8(8)
+  }
+#undef FATHOM_SCAN_CASE4
+#undef FATHOM_SCAN_CASE8
+#undef FATHOM_SCAN_LAUNCH
   return set_error(FATHOM_ERR_UNSUPPORTED, "scan: G=%d", G);
+}
+}  // namespace
+}  // namespace fathom
+
+extern "C" int fathom_scan(const float* q, int64_t BH, int G, int64_t n, int64_t sub, const int32_t* cls,
+                           const int32_t* clsn, int bmax, const uint64_t* planes_k, const uint16_t* scales_k,
+                           int64_t blk_begin, int64_t blk_end, float* scores, void* stream) {
+  return scan_dispatch(q, BH, G, n, sub, cls, clsn, bmax, planes_k, scales_k, blk_begin, blk_end, scores, nullptr,
+                       reinterpret_cast<cudaStream_t>(stream));
+}
+
+extern "C" size_t fathom_scan_select_workspace_bytes(int64_t BH, int G, int64_t n, int64_t kk) {
+  (void)n;
+  (void)kk;
+  return BH > 0 && G > 0 ? selectk::ws_bytes(BH * G) : 0;
+}
+
+extern "C" int fathom_scan_select(const float* q, int64_t BH, int G, int64_t n, int64_t sub, const int32_t* cls,
+                                  const int32_t* clsn, int bmax, const uint64_t* planes_k, const uint16_t* scales_k,
+                                  int64_t kk, int64_t mask_lo, int64_t mask_hi, int64_t index_offset,
+                                  int64_t append_sink, int64_t append_local, float* scores, int64_t* out_idx,
+                                  int64_t out_stride, float* out_scores, void* workspace, size_t workspace_bytes,
+                                  void* scan_done_event, void* stream) {
+  const int64_t rows = BH * G;
+  FATHOM_REQUIRE(out_idx && workspace, FATHOM_ERR_NULL, "scan_select: NULL pointer");
+  FATHOM_REQUIRE(kk >= 1 && kk <= selectk::MAX_KK && kk <= n && n <= 0xffffffffLL, FATHOM_ERR_SHAPE,
+                 "scan_select: kk=%lld outside 1..min(4096, n=%lld)", (long long)kk, (long long)n);
+  FATHOM_REQUIRE(append_sink >= 0 && append_local >= 0 && out_stride >= kk + append_sink + append_local,
+                 FATHOM_ERR_SHAPE, "scan_select: bad output stride");
+  FATHOM_REQUIRE(workspace_bytes >= selectk::ws_bytes(rows) && (reinterpret_cast<uintptr_t>(workspace) & 255) == 0,
+                 FATHOM_ERR_WORKSPACE, "scan_select: workspace needs %zu bytes, 256-byte aligned",
+                 selectk::ws_bytes(rows));
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  selectk::Workspace w = selectk::carve(workspace, rows);
+  cudaError_t e = cudaMemsetAsync(workspace, 0, selectk::zeroed_bytes(rows), st);
+  if (e != cudaSuccess) return set_error(FATHOM_ERR_CUDA, "scan_select: memset: %s", cudaGetErrorString(e));
+  HistArgs ha{mask_lo, mask_hi, kk, w.hist, w.ticket, w.bstar};
+  const int64_t nblk = cdiv(n, BLK);
+  int r = scan_dispatch(q, BH, G, n, sub, cls, clsn, bmax, planes_k, scales_k, 0, nblk, scores, &ha, st);
+  if (r != FATHOM_OK) return r;
+  if (scan_done_event) {
+    e = cudaEventRecord(reinterpret_cast<cudaEvent_t>(scan_done_event), st);
+    if (e != cudaSuccess) return set_error(FATHOM_ERR_CUDA, "scan_select: event record: %s", cudaGetErrorString(e));
+  }
+  return selectk::launch_select_tail(scores, rows, n, n, kk, mask_lo, mask_hi, index_offset, out_idx, out_stride,
+                                     out_scores, append_sink, append_local, w, st);
 }

@@ -4,141 +4,135 @@
 // Output order is (score descending, index ascending); every tie is broken by the index, so
 // the selection is deterministic and a context-sharded scan merges to the same list.
 //
-// Fast path, three launches on the caller's stream:
+// Three launches on the caller's stream:
 //   1 hist      many CTAs per row: 4096-bin histogram of the top 12 bits of the order-
 //               preserving key of every unmasked score (masked tokens get the key of -inf);
 //               shared-memory histogram, flushed to the row's global histogram with atomics.
-//   2 collect   many CTAs per row: each finds the boundary bin b* (the largest bin with at least
-//               kk keys at or above it) from the global histogram, then appends every key in
-//               bins >= b* as a 64-bit (key << 32 | ~index) candidate, warp-aggregated atomics.
-//   3 finalize  one CTA per row: bitonic sort of the candidates in shared memory, descending
-//               on (key, ~index), then the first kk.  If a row has more candidates than the
-//               buffer holds (massive ties, or kk close to n) it switches to an exact radix
-//               select over the whole row (12+12+8 bits) and an index-ordered compaction of
-//               the keys equal to the threshold.
-#include "common.cuh"
+//               The last CTA of a row (atomic ticket; nothing waits) derives the boundary bin b*:
+//               the largest bin with at least kk keys at or above it.
+//   2 collect   many CTAs per row: appends every key in bins >= b* as a 64-bit candidate
+//               (key << 32 | ~index), warp-aggregated atomics.  Candidates are unique and their
+//               descending order is (score desc, index asc).
+//   3 finalize  one CTA per row: radix select of the kk-th largest candidate on the remaining
+//               52 bits (12-bit digits in shared memory, stopping as soon as the prefix holds
+//               exactly the number still needed), compaction of exactly kk candidates, bitonic
+//               sort of those.  A row with more candidates than the buffer holds (massive ties,
+//               or kk close to n) takes an exact radix select over the whole row (12+12+8 bits)
+//               and an index-ordered compaction of the keys equal to the threshold.
+#include "select_common.cuh"
 
 #include <atomic>
 
 namespace fathom {
+using namespace selectk;
 namespace {
-
-constexpr int HBITS = 12;
-constexpr int NBINS = 1 << HBITS;
-constexpr int CAP = 8192;          // candidates kept per row in the fast path
-constexpr int MAX_KK = 4096;
-constexpr int CHUNK = 16384;       // scores per CTA in the hist / collect passes
-constexpr int HT = 512;            // threads of hist / collect CTAs
-constexpr int FT = 1024;           // threads of the finalize CTA
-
-struct Workspace {
-  uint32_t* hist;   // [rows][NBINS]
-  uint32_t* count;  // [rows]
-  uint64_t* cand;   // [rows][CAP]
-};
-
-size_t align256(size_t x) { return (x + 255) & ~(size_t)255; }
-
-size_t ws_bytes(int64_t rows) {
-  return align256(rows * NBINS * sizeof(uint32_t)) + align256(rows * sizeof(uint32_t)) +
-         align256(rows * (size_t)CAP * sizeof(uint64_t));
-}
-
-Workspace carve(void* base, int64_t rows) {
-  char* p = static_cast<char*>(base);
-  Workspace w;
-  w.hist = reinterpret_cast<uint32_t*>(p);
-  p += align256(rows * NBINS * sizeof(uint32_t));
-  w.count = reinterpret_cast<uint32_t*>(p);
-  p += align256(rows * sizeof(uint32_t));
-  w.cand = reinterpret_cast<uint64_t*>(p);
-  return w;
-}
 
 __device__ __forceinline__ uint32_t masked_key(const float* row, int64_t i, int64_t mask_lo, int64_t mask_hi) {
   return (i >= mask_lo && i < mask_hi) ? f2key(row[i]) : KEY_NEG_INF;
 }
 
+// Scores i0..i1 of a row, four at a time when the row is 16-byte aligned.
+template <typename F>
+__device__ __forceinline__ void for_each_score(const float* r, int64_t i0, int64_t i1, bool vec, F&& f) {
+  if (vec) {
+    for (int64_t i = i0 + 4 * (int64_t)threadIdx.x; i < i1; i += 4 * (int64_t)blockDim.x) {
+      const float4 v = *reinterpret_cast<const float4*>(r + i);
+      f(i, v.x);
+      if (i + 1 < i1) f(i + 1, v.y);
+      if (i + 2 < i1) f(i + 2, v.z);
+      if (i + 3 < i1) f(i + 3, v.w);
+    }
+  } else {
+    for (int64_t i = i0 + threadIdx.x; i < i1; i += blockDim.x) f(i, r[i]);
+  }
+}
+
 __global__ void __launch_bounds__(HT) hist_kernel(const float* __restrict__ scores, int64_t n, int64_t row_stride,
-                                                  int64_t mask_lo, int64_t mask_hi, uint32_t* __restrict__ ghist) {
+                                                  int64_t kk, int64_t mask_lo, int64_t mask_hi,
+                                                  uint32_t* __restrict__ ghist, uint32_t* __restrict__ ticket,
+                                                  uint32_t* __restrict__ bstar) {
   __shared__ uint32_t sh[NBINS];
+  __shared__ uint32_t s_part[HT];
+  __shared__ int s_res;
+  __shared__ bool s_last;
   const int64_t row = blockIdx.y;
   for (int b = threadIdx.x; b < NBINS; b += HT) sh[b] = 0;
   __syncthreads();
   const float* r = scores + row * row_stride;
   const int64_t i0 = (int64_t)blockIdx.x * CHUNK;
   const int64_t i1 = i0 + CHUNK < n ? i0 + CHUNK : n;
-  for (int64_t i = i0 + threadIdx.x; i < i1; i += HT) atomicAdd(&sh[masked_key(r, i, mask_lo, mask_hi) >> (32 - HBITS)], 1u);
+  const bool vec = (n % 4 == 0) && (row_stride % 4 == 0) && ((reinterpret_cast<uintptr_t>(scores) & 15) == 0);
+  for_each_score(r, i0, i1, vec, [&](int64_t i, float x) {
+    const uint32_t key = (i >= mask_lo && i < mask_hi) ? f2key(x) : KEY_NEG_INF;
+    atomicAdd(&sh[key >> (32 - HBITS)], 1u);
+  });
   __syncthreads();
   uint32_t* gh = ghist + row * NBINS;
   for (int b = threadIdx.x; b < NBINS; b += HT)
     if (sh[b]) atomicAdd(&gh[b], sh[b]);
-}
-
-// Boundary bin from a row histogram held in shared memory, with `nt` threads (multiple of 32).
-// Returns (to every thread) the largest bin b with sum_{b' >= b} hist[b'] >= kk.
-__device__ int boundary_bin(const uint32_t* s_hist, int64_t kk, uint32_t* s_part, int* s_res) {
-  const int nt = blockDim.x;
-  const int per = NBINS / nt;
-  const int t = threadIdx.x;
-  uint32_t part = 0;
-  for (int b = 0; b < per; ++b) part += s_hist[t * per + b];
-  s_part[t] = part;
+  // the last CTA of the row to finish derives the boundary bin (no CTA waits for another)
+  __threadfence();
   __syncthreads();
-  // inclusive suffix sums over threads (Hillis-Steele on shared memory)
-  for (int o = 1; o < nt; o <<= 1) {
-    const uint32_t v = (t + o < nt) ? s_part[t + o] : 0u;
-    __syncthreads();
-    s_part[t] += v;
-    __syncthreads();
-  }
-  if (t == 0) *s_res = 0;
+  if (threadIdx.x == 0) s_last = atomicAdd(&ticket[row], 1u) == gridDim.x - 1;
   __syncthreads();
-  const uint32_t above = (t + 1 < nt) ? s_part[t + 1] : 0u;
-  if (s_part[t] >= (uint32_t)kk && above < (uint32_t)kk) {
-    uint32_t run = above;
-    for (int b = (t + 1) * per - 1; b >= t * per; --b) {
-      run += s_hist[b];
-      if (run >= (uint32_t)kk) {
-        *s_res = b;
-        break;
-      }
-    }
-  }
+  if (!s_last) return;
+  __threadfence();
+  for (int b = threadIdx.x; b < NBINS; b += HT) sh[b] = __ldcg(&gh[b]);
   __syncthreads();
-  return *s_res;
+  const int bs = boundary_bin(sh, kk, s_part, &s_res);
+  if (threadIdx.x == 0) bstar[row] = (uint32_t)bs;
 }
 
 __global__ void __launch_bounds__(HT) collect_kernel(const float* __restrict__ scores, int64_t n, int64_t row_stride,
-                                                     int64_t kk, int64_t mask_lo, int64_t mask_hi,
-                                                     const uint32_t* __restrict__ ghist, uint32_t* __restrict__ count,
-                                                     uint64_t* __restrict__ cand) {
-  __shared__ uint32_t s_hist[NBINS];
-  __shared__ uint32_t s_part[HT];
-  __shared__ int s_res;
+                                                     int64_t mask_lo, int64_t mask_hi,
+                                                     const uint32_t* __restrict__ bstar_rows,
+                                                     uint32_t* __restrict__ count, uint64_t* __restrict__ cand) {
+  constexpr int PER = CHUNK / HT;           // scores per thread (32)
   const int64_t row = blockIdx.y;
-  for (int b = threadIdx.x; b < NBINS; b += HT) s_hist[b] = ghist[row * NBINS + b];
-  __syncthreads();
-  const uint32_t bstar = (uint32_t)boundary_bin(s_hist, kk, s_part, &s_res);
+  const uint32_t bstar = bstar_rows[row];
   const float* r = scores + row * row_stride;
   const int64_t i0 = (int64_t)blockIdx.x * CHUNK;
   const int64_t i1 = i0 + CHUNK < n ? i0 + CHUNK : n;
   const int lane = threadIdx.x & 31;
   uint64_t* cr = cand + row * CAP;
-  for (int64_t base = i0; base < i1; base += HT) {
-    const int64_t i = base + threadIdx.x;
-    uint32_t key = 0;
-    bool take = false;
-    if (i < i1) {
-      key = masked_key(r, i, mask_lo, mask_hi);
-      take = (key >> (32 - HBITS)) >= bstar;
+  const bool vec = (n % 4 == 0) && (row_stride % 4 == 0) && ((reinterpret_cast<uintptr_t>(scores) & 15) == 0);
+  // all loads of this thread first (thread t owns scores i0 + 4t + 4*HT*u + e), then the filter
+  float x[PER];
+  if (vec) {
+#pragma unroll
+    for (int u = 0; u < PER / 4; ++u) {
+      const int64_t i = i0 + 4 * ((int64_t)threadIdx.x + (int64_t)u * HT);
+      const float4 v = i < i1 ? *reinterpret_cast<const float4*>(r + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+      x[4 * u] = v.x; x[4 * u + 1] = v.y; x[4 * u + 2] = v.z; x[4 * u + 3] = v.w;
     }
+  } else {
+#pragma unroll
+    for (int u = 0; u < PER; ++u) {
+      const int64_t i = i0 + 4 * ((int64_t)threadIdx.x + (int64_t)(u / 4) * HT) + (u % 4);
+      x[u] = i < i1 ? r[i] : 0.f;
+    }
+  }
+  // which of this thread's scores are candidates (a bit per score); most warps have none
+  const bool unmasked = i0 >= mask_lo && i1 <= mask_hi;   // the whole chunk is outside sink/local
+  uint32_t takes = 0;
+#pragma unroll
+  for (int u = 0; u < PER; ++u) {
+    const int64_t i = i0 + 4 * ((int64_t)threadIdx.x + (int64_t)(u / 4) * HT) + (u % 4);
+    const uint32_t key = (unmasked || (i >= mask_lo && i < mask_hi)) ? f2key(x[u]) : KEY_NEG_INF;
+    if (i < i1 && (key >> (32 - HBITS)) >= bstar) takes |= 1u << u;
+  }
+  if (!__any_sync(0xffffffffu, takes != 0)) return;
+#pragma unroll
+  for (int u = 0; u < PER; ++u) {
+    const int64_t i = i0 + 4 * ((int64_t)threadIdx.x + (int64_t)(u / 4) * HT) + (u % 4);
+    const bool take = (takes >> u) & 1u;
     const uint32_t m = __ballot_sync(0xffffffffu, take);
     if (m) {
       uint32_t pos0 = 0;
       if (lane == 0) pos0 = atomicAdd(&count[row], (uint32_t)__popc(m));
       pos0 = __shfl_sync(0xffffffffu, pos0, 0);
       if (take) {
+        const uint32_t key = (unmasked || (i >= mask_lo && i < mask_hi)) ? f2key(x[u]) : KEY_NEG_INF;
         const uint32_t pos = pos0 + __popc(m & ((1u << lane) - 1));
         if (pos < CAP) cr[pos] = ((uint64_t)key << 32) | (uint32_t)(~(uint32_t)i);
       }
@@ -170,36 +164,6 @@ __device__ __forceinline__ int next_pow2(int x) {
   int p = 1;
   while (p < x) p <<= 1;
   return p;
-}
-
-// Block-wide exclusive scan of one value per thread (blockDim.x <= 1024). Returns the prefix;
-// *total receives the block sum.
-__device__ uint32_t block_exclusive_scan(uint32_t v, uint32_t* s_warp, uint32_t* total) {
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
-  uint32_t x = v;
-#pragma unroll
-  for (int o = 1; o < 32; o <<= 1) {
-    const uint32_t y = __shfl_up_sync(0xffffffffu, x, o);
-    if (lane >= o) x += y;
-  }
-  if (lane == 31) s_warp[warp] = x;
-  __syncthreads();
-  if (warp == 0) {
-    uint32_t w = lane < nw ? s_warp[lane] : 0u;
-    uint32_t z = w;
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-      const uint32_t y = __shfl_up_sync(0xffffffffu, z, o);
-      if (lane >= o) z += y;
-    }
-    if (lane < nw) s_warp[lane] = z - w;
-    if (lane == 31) s_warp[32] = z;
-  }
-  __syncthreads();
-  const uint32_t res = s_warp[warp] + x - v;
-  *total = s_warp[32];
-  __syncthreads();
-  return res;
 }
 
 // Exact selection of the kk largest keys of one row by a single CTA (rare path).  Writes the
@@ -253,14 +217,51 @@ __device__ void exact_select_row(const float* r, int64_t n, int64_t kk, int64_t 
   __syncthreads();
 }
 
+// Radix select on 64-bit candidates held in shared memory: returns (to every thread) the
+// smallest value C such that exactly kk of the n values are >= C.  The values are unique; the
+// top 12 bits of the kk-th largest are `top12` and `need` of the values equal it in those bits.
+__device__ uint64_t refine_threshold(const uint64_t* s_v, int n, uint32_t top12, int64_t need, uint32_t* s_hist,
+                                     uint32_t* s_part, int* s_res, uint32_t* s_warp) {
+  uint64_t prefix = (uint64_t)top12 << 52;
+  uint64_t pmask = 0xFFFull << 52;
+  const int shifts[5] = {40, 28, 16, 4, 0};
+  const int widths[5] = {12, 12, 12, 12, 4};
+  for (int lv = 0; lv < 5; ++lv) {
+    // values still matching the prefix
+    uint32_t cnt = 0;
+    for (int i = threadIdx.x; i < n; i += blockDim.x) cnt += (s_v[i] & pmask) == prefix;
+    uint32_t tot;
+    block_exclusive_scan(cnt, s_warp, &tot);
+    if ((int64_t)tot == need) break;
+    const int sh = shifts[lv], nb = 1 << widths[lv];
+    for (int b = threadIdx.x; b < NBINS; b += blockDim.x) s_hist[b] = 0;
+    __syncthreads();
+    for (int i = threadIdx.x; i < n; i += blockDim.x)
+      if ((s_v[i] & pmask) == prefix) atomicAdd(&s_hist[(s_v[i] >> sh) & (nb - 1)], 1u);
+    __syncthreads();
+    const int b = boundary_bin(s_hist, need, s_part, s_res);
+    uint32_t above = 0;
+    for (int x = threadIdx.x; x < NBINS; x += blockDim.x)
+      if (x > b) above += s_hist[x];
+    block_exclusive_scan(above, s_warp, &tot);
+    need -= tot;
+    prefix |= (uint64_t)b << sh;
+    pmask |= (uint64_t)(nb - 1) << sh;
+  }
+  return prefix;
+}
+
 __global__ void __launch_bounds__(FT) finalize_kernel(const float* __restrict__ scores, int64_t n, int64_t row_stride,
                                                       int64_t kk, int64_t mask_lo, int64_t mask_hi,
                                                       const uint32_t* __restrict__ count,
+                                                      const uint32_t* __restrict__ bstar_rows,
                                                       const uint64_t* __restrict__ cand, int64_t index_offset,
                                                       int64_t* __restrict__ out_idx, int64_t out_stride,
                                                       float* __restrict__ out_scores, int64_t append_sink,
                                                       int64_t append_local) {
-  extern __shared__ uint64_t s_buf[];  // CAP entries
+  extern __shared__ uint64_t s_dyn[];  // CAP candidates, then MAX_KK selected
+  uint64_t* s_buf = s_dyn;
+  uint64_t* s_sel = s_dyn + CAP;
   __shared__ uint32_t s_hist[NBINS];
   __shared__ uint32_t s_part[FT];
   __shared__ uint32_t s_warp[33];
@@ -268,21 +269,33 @@ __global__ void __launch_bounds__(FT) finalize_kernel(const float* __restrict__ 
   __shared__ int s_res;
   const int64_t row = blockIdx.x;
   const uint32_t cnt = count[row];
-  int P;
   if (cnt <= (uint32_t)CAP) {
-    P = next_pow2((int)cnt);
-    for (int i = threadIdx.x; i < P; i += blockDim.x) s_buf[i] = i < (int)cnt ? cand[row * CAP + i] : 0ull;
+    const uint32_t top12 = bstar_rows[row];
+    uint32_t above = 0;
+    for (int i = threadIdx.x; i < (int)cnt; i += blockDim.x) {
+      const uint64_t v = cand[row * CAP + i];
+      s_buf[i] = v;
+      above += (uint32_t)(v >> 52) > top12;
+    }
+    uint32_t tot;
+    block_exclusive_scan(above, s_warp, &tot);  // also orders the loads above before the reads below
+    const uint64_t C = refine_threshold(s_buf, (int)cnt, top12, kk - (int64_t)tot, s_hist, s_part, &s_res, s_warp);
+    if (threadIdx.x == 0) s_cnt = 0;
+    __syncthreads();
+    for (int i = threadIdx.x; i < (int)cnt; i += blockDim.x)
+      if (s_buf[i] >= C) s_sel[atomicAdd(&s_cnt, 1u)] = s_buf[i];
     __syncthreads();
   } else {
-    exact_select_row(scores + row * row_stride, n, kk, mask_lo, mask_hi, s_buf, s_hist, s_part, &s_res, s_warp, &s_cnt);
-    P = next_pow2((int)kk);
-    for (int i = (int)kk + threadIdx.x; i < P; i += blockDim.x) s_buf[i] = 0ull;
-    __syncthreads();
+    exact_select_row(scores + row * row_stride, n, kk, mask_lo, mask_hi, s_sel, s_hist, s_part, &s_res, s_warp,
+                     &s_cnt);
   }
-  bitonic_desc(s_buf, P);
+  const int P = next_pow2((int)kk);
+  for (int i = (int)kk + threadIdx.x; i < P; i += blockDim.x) s_sel[i] = 0ull;
+  __syncthreads();
+  bitonic_desc(s_sel, P);
   int64_t* o = out_idx + row * out_stride;
   for (int i = threadIdx.x; i < kk; i += blockDim.x) {
-    const uint64_t v = s_buf[i];
+    const uint64_t v = s_sel[i];
     o[i] = (int64_t)(uint32_t)(~(uint32_t)v) + index_offset;
     if (out_scores) out_scores[row * kk + i] = key2f((uint32_t)(v >> 32));
   }
@@ -322,26 +335,33 @@ int run_select(const float* scores, int64_t rows, int64_t n, int64_t row_stride,
                  FATHOM_ERR_WORKSPACE, "select_topk: workspace needs %zu bytes, 256-byte aligned (got %zu)",
                  ws_bytes(rows), workspace_bytes);
   Workspace w = carve(workspace, rows);
-  cudaError_t e = cudaMemsetAsync(workspace, 0, reinterpret_cast<char*>(w.cand) - static_cast<char*>(workspace), st);
+  cudaError_t e = cudaMemsetAsync(workspace, 0, zeroed_bytes(rows), st);
   if (e != cudaSuccess) return set_error(FATHOM_ERR_CUDA, "select_topk: memset: %s", cudaGetErrorString(e));
   const int64_t chunks = cdiv(n, CHUNK);
   dim3 grid((unsigned)chunks, (unsigned)rows);
-  hist_kernel<<<grid, HT, 0, st>>>(scores, n, row_stride, mask_lo, mask_hi, w.hist);
-  collect_kernel<<<grid, HT, 0, st>>>(scores, n, row_stride, kk, mask_lo, mask_hi, w.hist, w.count, w.cand);
-  const size_t smem = CAP * sizeof(uint64_t);
-  static bool attr_set = false;
-  if (!attr_set) {
-    cudaFuncSetAttribute(finalize_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    cudaFuncSetAttribute(merge_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    attr_set = true;
-  }
-  finalize_kernel<<<(unsigned)rows, FT, smem, st>>>(scores, n, row_stride, kk, mask_lo, mask_hi, w.count, w.cand,
-                                                     index_offset, out_idx, out_stride, out_scores, append_sink,
-                                                     append_local);
-  return check_launch("select_topk");
+  hist_kernel<<<grid, HT, 0, st>>>(scores, n, row_stride, kk, mask_lo, mask_hi, w.hist, w.ticket, w.bstar);
+  return launch_select_tail(scores, rows, n, row_stride, kk, mask_lo, mask_hi, index_offset, out_idx, out_stride,
+                            out_scores, append_sink, append_local, w, st);
 }
 
 }  // namespace
+
+namespace selectk {
+int launch_select_tail(const float* scores, int64_t rows, int64_t n, int64_t row_stride, int64_t kk, int64_t mask_lo,
+                       int64_t mask_hi, int64_t index_offset, int64_t* out_idx, int64_t out_stride,
+                       float* out_scores, int64_t append_sink, int64_t append_local, const Workspace& w,
+                       cudaStream_t st) {
+  const int64_t chunks = cdiv(n, CHUNK);
+  dim3 grid((unsigned)chunks, (unsigned)rows);
+  collect_kernel<<<grid, HT, 0, st>>>(scores, n, row_stride, mask_lo, mask_hi, w.bstar, w.count, w.cand);
+  const size_t smem = (CAP + MAX_KK) * sizeof(uint64_t);
+  cudaFuncSetAttribute(finalize_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  finalize_kernel<<<(unsigned)rows, FT, smem, st>>>(scores, n, row_stride, kk, mask_lo, mask_hi, w.count, w.bstar,
+                                                     w.cand, index_offset, out_idx, out_stride, out_scores,
+                                                     append_sink, append_local);
+  return check_launch("select_topk");
+}
+}  // namespace selectk
 }  // namespace fathom
 
 using namespace fathom;
@@ -395,11 +415,7 @@ extern "C" int fathom_merge_topk(const float* cand_scores, const int64_t* cand_i
 namespace fathom {
 namespace {
 
-constexpr size_t static_align256(size_t x) { return (x + 255) & ~(size_t)255; }
-constexpr size_t kStaticScratchBytes =
-    static_align256((size_t)FATHOM_STATIC_TOPK_MAX_ROWS * NBINS * sizeof(uint32_t)) +
-    static_align256((size_t)FATHOM_STATIC_TOPK_MAX_ROWS * sizeof(uint32_t)) +
-    static_align256((size_t)FATHOM_STATIC_TOPK_MAX_ROWS * CAP * sizeof(uint64_t));
+constexpr size_t kStaticScratchBytes = ws_bytes(FATHOM_STATIC_TOPK_MAX_ROWS);
 
 static __device__ __align__(256) unsigned char g_topk_scratch[kStaticScratchBytes];
 

@@ -44,14 +44,17 @@ class MappedBuffer:
     .host  CPU tensor view of the memory (for filling / checking on the host)
     .dev   CUDA tensor aliasing the same memory through its device address: kernels that read it
            pull the bytes over the host link (zero-copy)
-    Freed with .free() or when garbage-collected."""
+    hugepages=True backs it with 2 MB transparent huge pages (cudaHostRegister) instead of
+    cudaHostAlloc.  Freed with .free() or when garbage-collected."""
 
-    def __init__(self, shape, dtype, device=None):
+    def __init__(self, shape, dtype, device=None, hugepages=False):
         self.shape, self.dtype = tuple(shape), dtype
         elem = torch.empty((), dtype=dtype).element_size()
         self.nbytes = int(math.prod(self.shape)) * elem
         hp, dp = ctypes.c_void_p(), ctypes.c_void_p()
-        check(lib().fathom_host_alloc_mapped(self.nbytes, ctypes.byref(hp), ctypes.byref(dp)), "host_alloc_mapped")
+        flags = _lib.HOST_HUGEPAGES if hugepages else 0
+        check(lib().fathom_host_alloc_mapped_ex(self.nbytes, flags, ctypes.byref(hp), ctypes.byref(dp)),
+              "host_alloc_mapped")
         self.hp, self.dp = hp.value, dp.value
         raw = (ctypes.c_byte * self.nbytes).from_address(self.hp)
         self.host = torch.frombuffer(raw, dtype=dtype).view(self.shape)
@@ -103,7 +106,7 @@ class HostPlaneStore(bp.PlaneStore):
     released.  scan() reads the host memory directly (zero-copy), with the same kernel as the HBM
     store."""
 
-    def __init__(self, K, scale_dtype=torch.float16):
+    def __init__(self, K, scale_dtype=torch.float16, hugepages=False):
         require_cuda(K)
         old = bp.SUB
         try:
@@ -111,8 +114,8 @@ class HostPlaneStore(bp.PlaneStore):
             super().__init__(K, scale_dtype)
         finally:
             bp.SUB = old
-        self.planes_buf = MappedBuffer(self.planes_k.shape, torch.int64, K.device)
-        self.scales_buf = MappedBuffer(self.scales_k.shape, torch.float16, K.device)
+        self.planes_buf = MappedBuffer(self.planes_k.shape, torch.int64, K.device, hugepages)
+        self.scales_buf = MappedBuffer(self.scales_k.shape, torch.float16, K.device, hugepages)
         self.planes_buf.dev.copy_(self.planes_k)
         self.scales_buf.dev.copy_(self.scales_k)
         torch.cuda.current_stream(K.device).synchronize()
@@ -138,6 +141,11 @@ def gather_rows(src, cap, idx, BH, dtype=torch.bfloat16, D=128):
     return dst
 
 
+def _row_stride(t):
+    """Elements between consecutive rows of a K/V source (128 unless it is a strided tensor view)."""
+    return t.stride(-2) if isinstance(t, torch.Tensor) and t.dim() >= 2 else 0
+
+
 def decode_attention(q, idx, K_src, V_src, cap, n_host=None, K_recent=None, V_recent=None, recent_cap=0,
                      out_dtype=torch.float32):
     """Exact attention over the selected rows (scripts/B_e2e_offload_v2.py:226-244):
@@ -155,7 +163,8 @@ def decode_attention(q, idx, K_src, V_src, cap, n_host=None, K_recent=None, V_re
     if out_dtype not in (torch.float32, torch.bfloat16):
         raise TypeError("decode_attention: out_dtype must be float32 or bfloat16")
     ws = _lib.workspace(dev, lib().fathom_decode_workspace_bytes(BH, G, k), "decode")
-    check(lib().fathom_decode_attention(ptr(qc), BH, G, ptr(ic), k, ptr(K_src), ptr(V_src), cap, n_host,
+    check(lib().fathom_decode_attention(ptr(qc), BH, G, ptr(ic), k, ptr(K_src), ptr(V_src), cap,
+                                        _row_stride(K_src), n_host,
                                         ptr(K_recent), ptr(V_recent), recent_cap,
                                         ptr(out) if out_dtype == torch.float32 else None,
                                         ptr(out) if out_dtype == torch.bfloat16 else None,
@@ -169,8 +178,7 @@ def decode_step(q, g, budget, store, K_src, V_src, cap, k=580, sink=4, local=64,
     method): plan -> plane-prefix scan of the (host or HBM) store -> sink+local top-k -> unique-row
     gather + exact attention.  Returns (out [BH,G,128], idx [BH,G,k])."""
     plan = bp.make_plan(g, budget)
-    s = store.scan(q, plan, out=scores)
-    idx = bp.sink_local_topk(s, k, sink, local)
+    idx = bp.scan_topk(store, q, plan, k, sink, local, scores=scores)
     out = decode_attention(q, idx, K_src, V_src, cap, n_host, K_recent, V_recent, recent_cap, out_dtype)
     return out, idx
 
@@ -186,7 +194,8 @@ def decode_attention_partial(q, idx, K_src, V_src, cap, idx_lo, idx_hi):
     ic = idx.contiguous().to(torch.int64)
     out = torch.empty(BH, G, D + 2, device=dev, dtype=torch.float32)
     ws = _lib.workspace(dev, lib().fathom_decode_partial_workspace_bytes(BH, G, k), "decode_partial")
-    check(lib().fathom_decode_attention_partial(ptr(qc), BH, G, ptr(ic), k, ptr(K_src), ptr(V_src), cap, idx_lo, idx_hi,
+    check(lib().fathom_decode_attention_partial(ptr(qc), BH, G, ptr(ic), k, ptr(K_src), ptr(V_src), cap,
+                                                _row_stride(K_src), idx_lo, idx_hi,
                                                 ptr(out), ptr(ws), ws.numel(), stream_of(dev)),
           "decode_attention_partial")
     return out

@@ -60,18 +60,24 @@ def all_gather(t, group=None):
 def sharded_select(scores, kk, lo, hi, n_total, sink, local, select_fn=None, merge_fn=None, gather_fn=None):
     """Global top-kk indices [BH, G, kk] (int64, global) of a context-sharded score row set.
 
-    scores [BH, G, hi-lo] are this rank's chunk.  select_fn(scores, kk, mask_lo, mask_hi, offset) ->
-    (idx, vals); merge_fn(vals [..., m], idx [..., m], kk) -> idx; gather_fn(t) -> [W, *t.shape]."""
+    scores [BH, G, hi-lo] are this rank's chunk (or anything select_fn accepts).
+    select_fn(scores, kk, mask_lo, mask_hi, offset) -> (idx, vals); merge_fn(vals [..., m], idx [..., m],
+    kk) -> idx; gather_fn(t) -> [W, *t.shape]."""
     if select_fn is None:
         from .bitplane import select_topk
         select_fn = lambda s, k, a, b, off: select_topk(s, k, mask_lo=a, mask_hi=b, index_offset=off,
                                                         with_scores=True)
+    mlo, mhi = local_window(lo, hi, n_total, sink, local)
+    idx, vals = select_fn(scores, kk, mlo, mhi, lo)
+    return merge_shards(idx, vals, kk, merge_fn, gather_fn)
+
+
+def merge_shards(idx, vals, kk, merge_fn=None, gather_fn=None):
+    """All-gather of every rank's local (idx, vals) [BH, G, kk] and the merge to the global top-kk."""
     if merge_fn is None:
         from .bitplane import merge_topk
         merge_fn = lambda v, i, k: merge_topk(v, i, k)[0]
     gather_fn = gather_fn or all_gather
-    mlo, mhi = local_window(lo, hi, n_total, sink, local)
-    idx, vals = select_fn(scores, kk, mlo, mhi, lo)
     BH, G, _ = idx.shape
     packed = torch.stack([vals.float().view(torch.int32), idx.to(torch.int32)])      # one collective
     allp = gather_fn(packed)                                                        # [W, 2, BH, G, kk]
@@ -94,16 +100,19 @@ def sharded_decode_step(a, layers, kv, scores, outs, rank, world, q_in=None, g_i
         plan = bp.make_plan(g, a.budget)
         if scan_events is not None:
             e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e1.record()    # creates the handle; the library records it again right after the scan kernel
             e0.record()
-        s = lay.store.scan(q, plan, out=scores)
+        mlo, mhi = local_window(lo, hi, n_total, a.sink, a.local)
+        idx_l, vals_l, _ = bp.scan_select(lay.store, q, plan, a.k, mask_lo=mlo, mask_hi=mhi, index_offset=lo,
+                                          scores=scores, with_scores=True,
+                                          scan_done_event=e1 if scan_events is not None else None)
         if scan_events is not None:
-            e1.record()
             scan_events.append((e0, e1, lay.bytes))
-        top = sharded_select(s, a.k, lo, hi, n_total, a.sink, a.local)
+        top = merge_shards(idx_l, vals_l, a.k)
         BH, G, _ = top.shape
         fixed = fixed_indices(n_total, a.sink, a.local, top.device).expand(BH, G, -1)
         idx = torch.cat([top, fixed], -1)
-        kb, vb = kv[L % len(kv)]
-        part = off.decode_attention_partial(q, idx, kb.dev, vb.dev, a.ctx, lo, hi)
+        rows = kv[L % len(kv)]
+        part = off.decode_attention_partial(q, idx, rows["K"], rows["V"], a.ctx, lo, hi)
         outs[L] = off.attention_combine(all_gather(part))
     return outs

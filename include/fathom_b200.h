@@ -94,10 +94,30 @@ int fathom_make_plan(const float* g, const float* budget, int64_t BH, int bmax, 
  * of the depth-class lists, reading only the first t_j planes of channel j.
  *   q [BH][G][128] fp32, G in 1..8; cls/clsn from fathom_make_plan (stride bmax);
  *   planes_k/scales_k in order `sub`, device memory or a mapped host alias;
- *   tokens of blocks [blk_begin, blk_end) are written to scores [BH][G][n]; others untouched. */
+ *   tokens of blocks [blk_begin, blk_end) are written to scores [BH][G][n]; others untouched.
+ *   Channel ids are taken modulo 128 and class counts clamped to 0..128 (plans from
+ *   fathom_make_plan always satisfy both). */
 int fathom_scan(const float* q, int64_t BH, int G, int64_t n, int64_t sub, const int32_t* cls, const int32_t* clsn,
                 int bmax, const uint64_t* planes_k, const uint16_t* scales_k, int64_t blk_begin, int64_t blk_end,
                 float* scores, void* stream);
+
+/* Workspace bytes of fathom_scan_select. */
+size_t fathom_scan_select_workspace_bytes(int64_t BH, int G, int64_t n, int64_t kk);
+
+/* The scan fused with the histogram pass of the selection: PlaneStore.scan followed by
+ * sink_local_topk (kernels/bitplane.py:319-338, 372-378) in four launches (memset, scan with the
+ * histogram in its epilogue, collect, finalize) instead of six; the scores are not re-read for the
+ * histogram.  Writes scores [BH][G][n] (all blocks) and, per row r = bh*G+g, the top-kk of tokens in
+ * [mask_lo, mask_hi) plus index_offset to out_idx [r][out_stride] in (score desc, index asc) order,
+ * followed by 0..append_sink-1 and n-append_local..n-1; the selected scores to out_scores [r][kk] if
+ * not NULL.  sink_local_topk(k, sink, local) is kk = k-sink-local, mask [sink, n-local), offset 0,
+ * append (sink, local), out_stride k.  scan_done_event (a cudaEvent_t, may be NULL) is recorded on
+ * the stream right after the scan kernel, to time the scan alone. */
+int fathom_scan_select(const float* q, int64_t BH, int G, int64_t n, int64_t sub, const int32_t* cls,
+                       const int32_t* clsn, int bmax, const uint64_t* planes_k, const uint16_t* scales_k, int64_t kk,
+                       int64_t mask_lo, int64_t mask_hi, int64_t index_offset, int64_t append_sink,
+                       int64_t append_local, float* scores, int64_t* out_idx, int64_t out_stride, float* out_scores,
+                       void* workspace, size_t workspace_bytes, void* scan_done_event, void* stream);
 
 /* ---------------------------------------------------------------- selection */
 
@@ -145,7 +165,7 @@ int fathom_merge_topk(const float* cand_scores, const int64_t* cand_idx, int64_t
 /* ---------------------------------------------------------------- rows + attention */
 
 /* dst[bh][r][:] = src[bh][idx[bh][r]][:] for bf16 rows of D (D*2 a multiple of 16);
- * idx < 0 skips the row (no traffic, dst row untouched).  src may be a mapped host alias
+ * idx < 0 skips the row (no traffic, dst row untouched); so does idx >= cap.  src may be a mapped host alias
  * (gather_rows_kernel, scripts/B_e2e_offload_v2.py:73-83). */
 int fathom_gather_rows(const uint16_t* src, int64_t cap, const int32_t* idx, int64_t BH, int64_t R, int64_t D,
                        uint16_t* dst, void* stream);
@@ -157,14 +177,15 @@ size_t fathom_decode_workspace_bytes(int64_t BH, int G, int64_t k);
  * HBM twin gather_attn, scripts/B_kernel_bench.py:26-31):
  *   q [BH][G][128] fp32; idx [BH][G][k] int64 token indices.
  *   Each unique index of a KV head is fetched once.  Index < n_host reads row idx of
- *   K_src/V_src [BH][cap][128] bf16 (device memory or mapped host alias); index >= n_host
+ *   K_src/V_src [BH][cap] rows of 128 bf16, kv_row_stride elements apart (0 = 128; 256 for a cache
+ *   that interleaves each token's K and V rows), in device memory or a mapped host alias; index >= n_host
  *   reads row idx-n_host of K_recent/V_recent [BH][recent_cap][128] bf16 (device).
  *   out = softmax(q K_sel^T / sqrt(128)) V_sel in fp32 math, to out_f32 [BH][G][128]
- *   and/or out_bf16 (either may be NULL). */
+ *   and/or out_bf16 (either may be NULL).  Picks at or beyond n_host + recent_cap are ignored. */
 int fathom_decode_attention(const float* q, int64_t BH, int G, const int64_t* idx, int64_t k, const uint16_t* K_src,
-                            const uint16_t* V_src, int64_t cap, int64_t n_host, const uint16_t* K_recent,
-                            const uint16_t* V_recent, int64_t recent_cap, float* out_f32, uint16_t* out_bf16,
-                            void* workspace, size_t workspace_bytes, void* stream);
+                            const uint16_t* V_src, int64_t cap, int64_t kv_row_stride, int64_t n_host,
+                            const uint16_t* K_recent, const uint16_t* V_recent, int64_t recent_cap, float* out_f32,
+                            uint16_t* out_bf16, void* workspace, size_t workspace_bytes, void* stream);
 
 /* Workspace bytes of fathom_decode_attention_partial. */
 size_t fathom_decode_partial_workspace_bytes(int64_t BH, int G, int64_t k);
@@ -176,9 +197,9 @@ size_t fathom_decode_partial_workspace_bytes(int64_t BH, int G, int64_t k);
  * reference runs on one GPU); it splits the attention of offload_attn
  * (scripts/B_e2e_offload_v2.py:242-244) across context shards. */
 int fathom_decode_attention_partial(const float* q, int64_t BH, int G, const int64_t* idx, int64_t k,
-                                    const uint16_t* K_src, const uint16_t* V_src, int64_t cap, int64_t idx_lo,
-                                    int64_t idx_hi, float* out_packed, void* workspace, size_t workspace_bytes,
-                                    void* stream);
+                                    const uint16_t* K_src, const uint16_t* V_src, int64_t cap, int64_t kv_row_stride,
+                                    int64_t idx_lo, int64_t idx_hi, float* out_packed, void* workspace,
+                                    size_t workspace_bytes, void* stream);
 
 /* Log-sum-exp merge of P shards' packed partials [P][rows][130] -> out [rows][128] (fp32 and/or
  * bf16): out = sum_p o_p e^(m_p - M) / sum_p l_p e^(m_p - M), M = max_p m_p. */
@@ -191,7 +212,16 @@ int fathom_attention_combine(const float* parts, int64_t P, int64_t rows, float*
  * scripts/B_e2e_offload_v2.py:33-38, which calls cudaHostAlloc(flags=3) and
  * cudaHostGetDevicePointer through ctypes). */
 int fathom_host_alloc_mapped(size_t bytes, void** host_ptr, void** dev_ptr);
-/* free_host (scripts/B_e2e_offload_v2.py:39). */
+/* Flags of fathom_host_alloc_mapped_ex. */
+#define FATHOM_HOST_HUGEPAGES 1
+
+/* fathom_host_alloc_mapped with options.  FATHOM_HOST_HUGEPAGES: anonymous memory advised to use
+ * 2 MB transparent huge pages (size rounded up to 2 MB, pre-faulted), pinned and mapped with
+ * cudaHostRegister(Mapped | Portable), so the GPU translates fewer pages on random row reads.
+ * No reference counterpart (the reference allocates with cudaHostAlloc only). */
+int fathom_host_alloc_mapped_ex(size_t bytes, int flags, void** host_ptr, void** dev_ptr);
+
+/* free_host (scripts/B_e2e_offload_v2.py:39); frees either kind of mapped allocation. */
 int fathom_host_free(void* host_ptr);
 
 #ifdef __cplusplus

@@ -25,7 +25,7 @@ def test_library_loads_and_exports_every_declared_symbol():
     for name in names:
         assert hasattr(L, name), name
     assert set(names) == set(_lib.SIGNATURES), "ctypes signatures out of sync with the header"
-    assert L.fathom_abi_version() == 1
+    assert L.fathom_abi_version() == 2
 
 
 def test_null_and_shape_errors_are_status_codes():
@@ -42,7 +42,7 @@ def test_null_and_shape_errors_are_status_codes():
     assert L.fathom_select_topk(p, 4, 1000, 1000, 10, 0, 1000, 0, p, 10, None, ctypes.c_void_p(256), need - 1,
                                 None) == _lib.FATHOM_ERR_WORKSPACE
     assert L.fathom_merge_topk(p, p, 1, 9000, 10, p, None, None) == _lib.FATHOM_ERR_SHAPE
-    assert L.fathom_decode_attention(p, 2, 4, p, 20000, p, p, 10, 10, None, None, 0, p, None, p, 1 << 30,
+    assert L.fathom_decode_attention(p, 2, 4, p, 20000, p, p, 10, 0, 10, None, None, 0, p, None, p, 1 << 30,
                                      None) == _lib.FATHOM_ERR_UNSUPPORTED
     assert L.fathom_quantise_pack(p, 7, 1, 64, 64 * 128, 16, 1, None, None, 0, None, None, None) == \
         _lib.FATHOM_ERR_UNSUPPORTED

@@ -69,3 +69,63 @@ def test_decode_attention_recent_rows():
     f = lambda t: O.bf16_to_f32(t.view(torch.int16).numpy().view(np.uint16))
     ref = O.decode_attention(q.numpy(), f(K), f(V), idx.numpy(), f(Kr), f(Vr), n_host)
     assert np.abs(out.cpu().numpy() - ref).max() <= 1e-5 * np.abs(ref).max() + 1e-6
+
+
+@pytest.mark.parametrize("parts", [1, 2, 3, 4])
+def test_partial_attention_combine_equals_full(parts):
+    """Context shards: partial attention over owned picks + log-sum-exp combine == full attention."""
+    from fathom_b200 import shard
+    from fathom_b200.offload import attention_combine, decode_attention, decode_attention_partial
+    BH, G, k, n = 3, 4, 300, 9000
+    K, V = _kv(BH, n, 40 + parts)
+    g = torch.Generator().manual_seed(parts)
+    q = torch.randn(BH, G, 128, generator=g).cuda()
+    idx = torch.randint(0, n, (BH, G, k), generator=g).cuda()
+    full = decode_attention(q, idx, K.cuda(), V.cuda(), n)
+    packed = []
+    for lo, hi in shard.chunk_bounds(n, parts):
+        Kc, Vc = K[:, lo:hi].contiguous().cuda(), V[:, lo:hi].contiguous().cuda()
+        packed.append(decode_attention_partial(q, idx, Kc, Vc, hi - lo, lo, hi))
+    out = attention_combine(torch.stack(packed))
+    assert torch.allclose(out, full, rtol=1e-5, atol=1e-6 * float(full.abs().max()))
+
+
+def test_hugepage_buffers_gather_and_attention():
+    """Huge-page-backed mapped buffers (cudaHostRegister) read like cudaHostAlloc ones."""
+    from fathom_b200.offload import MappedBuffer, decode_attention, gather_rows
+    BH, cap = 2, 50000
+    K, V = _kv(BH, cap, 77)
+    kb, vb = MappedBuffer(K.shape, torch.bfloat16, hugepages=True), MappedBuffer(V.shape, torch.bfloat16, hugepages=True)
+    kb.host.copy_(K)
+    vb.host.copy_(V)
+    idx = torch.randint(0, cap, (BH, 300), dtype=torch.int32)
+    got = gather_rows(kb.dev, cap, idx.cuda(), BH)
+    assert np.array_equal(got.cpu().view(torch.int16).numpy(), O.gather_rows(K.view(torch.int16).numpy(), idx.numpy()))
+    q = torch.randn(BH, 4, 128)
+    pick = torch.randint(0, cap, (BH, 4, 200))
+    a = decode_attention(q.cuda(), pick.cuda(), kb.dev, vb.dev, cap)
+    b = decode_attention(q.cuda(), pick.cuda(), K.cuda(), V.cuda(), cap)
+    assert torch.equal(a, b)
+    kb.free()
+    vb.free()
+
+
+@pytest.mark.parametrize("where", ["device", "host"])
+def test_interleaved_kv_rows(where):
+    """A cache that interleaves each token's K and V rows ([BH][cap][2][128], row stride 256) gives
+    the same attention as separate K and V buffers."""
+    from fathom_b200.offload import MappedBuffer, decode_attention
+    BH, G, k, cap = 3, 4, 400, 20000
+    K, V = _kv(BH, cap, 11)
+    KV = torch.stack([K, V], 2)                               # [BH, cap, 2, 128]
+    if where == "device":
+        kv = KV.cuda()
+    else:
+        buf = MappedBuffer(KV.shape, torch.bfloat16)
+        buf.host.copy_(KV)
+        kv = buf.dev
+    q = torch.randn(BH, G, 128).cuda()
+    idx = torch.randint(0, cap, (BH, G, k)).cuda()
+    a = decode_attention(q, idx, kv[:, :, 0], kv[:, :, 1], cap)
+    b = decode_attention(q, idx, K.cuda(), V.cuda(), cap)
+    assert torch.equal(a, b)

@@ -49,7 +49,7 @@ def test_scan_random_vs_oracle(G, n):
     assert score_rel_err(s, ref) < 1e-5
 
 
-@pytest.mark.parametrize("budget", [0.0, 1.0, 48.0, 92.0, 512.0])
+@pytest.mark.parametrize("budget", [0.0, 1.0, 31.0, 33.0, 48.0, 65.0, 92.0, 130.0, 200.0, 300.0, 512.0])
 def test_scan_budgets(budget):
     from fathom_b200 import bitplane as bp
     from fathom_b200.synth import make_layer
@@ -115,3 +115,39 @@ def test_config0_scores_sample():
     got = s[np.asarray(meta["score_sample_idx"])]
     ref = np.asarray(meta["score_sample"], np.float32)
     assert np.abs(got - ref).max() / meta["score_max_abs"] < 1e-5
+
+
+@pytest.mark.parametrize("G,budget", [(7, 200.0), (8, 512.0), (3, 70.0)])
+def test_scan_wide_groups_many_batches(G, budget):
+    from fathom_b200 import bitplane as bp
+    from fathom_b200.synth import make_layer
+    d = make_layer(2, G, 2500, seed=G, layer=7, with_v=False)
+    st = bp.PlaneStore(d["K"].cuda())
+    plan = bp.make_plan(d["g"].cuda(), budget)
+    s = st.scan(d["q"].cuda(), plan).cpu().numpy()
+    code, sc = O.quantise_u4(d["K"].numpy())
+    ref = O.scan_scores(d["q"].numpy(), code, sc, plan["t"].cpu().numpy())
+    assert score_rel_err(s, ref) < 1e-5
+
+
+@pytest.mark.parametrize("tpl", ["8", "16", "32"])
+@pytest.mark.parametrize("G,n", [(4, 131072), (4, 777), (7, 20000), (1, 5000)])
+def test_scan_token_splits(tpl, G, n, monkeypatch):
+    """Every tokens-per-lane split (forced through FATHOM_SCAN_TPL) gives the oracle's scores and the
+    same fused selection."""
+    from fathom_b200 import bitplane as bp
+    from fathom_b200.synth import make_layer
+    monkeypatch.setenv("FATHOM_SCAN_TPL", tpl)
+    d = make_layer(2, G, n, seed=n + G, layer=3, with_v=False)
+    st = bp.PlaneStore(d["K"].cuda())
+    plan = bp.make_plan(d["g"].cuda(), 48.0)
+    q = d["q"].cuda()
+    s = st.scan(q, plan)
+    code, sc = O.quantise_u4(d["K"].numpy())
+    ref = O.scan_scores(d["q"].numpy(), code, sc, plan["t"].cpu().numpy())
+    assert score_rel_err(s.cpu().numpy(), ref) < 1e-5
+    k = min(580, n)
+    assert torch.equal(bp.scan_topk(st, q, plan, k, 4, 64), bp.sink_local_topk(s, k, 4, 64))
+    out = torch.full_like(s, 5.0)
+    st.scan(q, plan, out=out, blocks=(1, 3))
+    assert torch.equal(out[..., 64:192], s[..., 64:192]) and torch.all(out[..., :64] == 5.0)

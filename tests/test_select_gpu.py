@@ -101,3 +101,65 @@ def test_shard_merge_equals_single():
         ci.append(i)
     idx, _ = bp.merge_topk(torch.cat(cs, -1), torch.cat(ci, -1), kk)
     assert torch.equal(idx, full)
+
+
+@pytest.mark.parametrize("world", [2, 3, 8])
+def test_sharded_select_emulated_equals_single(world):
+    """shard.sharded_select with every rank emulated on this GPU (the collective is a stack of the
+    ranks' packed candidates): merged indices bit-exact vs the single-pass sink+local selection."""
+    from fathom_b200 import bitplane as bp, shard
+    g = torch.Generator().manual_seed(world)
+    n, kk, sink, local = 64 * 700, 512, 4, 64
+    s = torch.randn(8, 4, n, generator=g).cuda()
+    full = bp.sink_local_topk(s, kk + sink + local, sink, local)[..., :kk]
+    bounds = shard.chunk_bounds(n, world)
+    packs = []
+    def capture(t):
+        packs.append(t)
+        raise StopIteration
+    for lo, hi in bounds:
+        try:
+            shard.sharded_select(s[..., lo:hi], kk, lo, hi, n, sink, local, gather_fn=capture)
+        except StopIteration:
+            pass
+    allp = torch.stack(packs)
+    for lo, hi in bounds:
+        got = shard.sharded_select(s[..., lo:hi], kk, lo, hi, n, sink, local, gather_fn=lambda t: allp)
+        assert torch.equal(got, full)
+
+
+@pytest.mark.parametrize("G,n,k", [(4, 131072, 580), (4, 700, 100), (7, 33000, 2116), (1, 5000, 300), (8, 20000, 1000)])
+@pytest.mark.parametrize("sub", [16, "nblk"])
+def test_scan_topk_fused_equals_unfused(G, n, k, sub):
+    """The scan with the selection histogram in its epilogue selects exactly what scan + sink_local_topk
+    selects (same scores, same order)."""
+    import math
+    from fathom_b200 import bitplane as bp
+    from fathom_b200.synth import make_layer
+    d = make_layer(2, G, n, seed=G + n, with_v=False)
+    old = bp.SUB
+    try:
+        bp.SUB = math.ceil(n / 64) if sub == "nblk" else sub
+        st = bp.PlaneStore(d["K"].cuda())
+    finally:
+        bp.SUB = old
+    plan = bp.make_plan(d["g"].cuda(), 48.0)
+    q = d["q"].cuda()
+    s = st.scan(q, plan)
+    ref = bp.sink_local_topk(s, k, 4, 64)
+    got = bp.scan_topk(st, q, plan, k, 4, 64)
+    assert torch.equal(got, ref)
+    idx, vals, s2 = bp.scan_select(st, q, plan, 200, mask_lo=10, mask_hi=n - 5, index_offset=1000, with_scores=True)
+    r_idx, r_vals = bp.select_topk(s, 200, mask_lo=10, mask_hi=n - 5, index_offset=1000, with_scores=True)
+    assert torch.equal(s2, s) and torch.equal(idx, r_idx) and torch.equal(vals, r_vals)
+
+
+def test_scan_topk_all_ties():
+    """Budget 0: every score is 0 (massive ties, the exact whole-row path): lowest indices first."""
+    from fathom_b200 import bitplane as bp
+    from fathom_b200.synth import make_layer
+    d = make_layer(2, 4, 30000, seed=1, with_v=False)
+    st = bp.PlaneStore(d["K"].cuda())
+    plan = bp.make_plan(d["g"].cuda(), 0.0)
+    got = bp.scan_topk(st, d["q"].cuda(), plan, 580, 4, 64).cpu().numpy()
+    assert np.array_equal(got, O.sink_local_topk(np.zeros((2, 4, 30000), np.float32), 580, 4, 64))
