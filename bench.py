@@ -12,11 +12,10 @@ depends on the previous layer's output in a real model).
   value   scanned key-rows/s = T * Hkv * layers / step time, inputs (q, g) already on the device
   e2e     the same through the public API with host buffers: every step copies that step's
           queries and gains from pinned host memory and reads the attention outputs back
-  roofline  the scan kernel (with the selection histogram in its epilogue): algorithmic bytes
-          (bytes_planes of each layer's plan) / its mean CUDA-event duration (events recorded on the
-          launching stream around the kernel: before the call's memset, and by the library right
-          after the kernel), against the host link bandwidth measured in this run (pinned H2D
-          cudaMemcpy, 1 GiB)
+  roofline  the scan kernel: algorithmic bytes (bytes_planes of each layer's plan) / its mean
+          CUDA-event duration (events recorded on the launching stream right before the scan call and,
+          by the library, right after the scan kernel), against the host link bandwidth measured in
+          this run (pinned H2D cudaMemcpy, 1 GiB)
   hbm_resident  config 1 (T = 131072, index + K/V in HBM) as a secondary figure, against
           MEASURED_PEAKS.json hbm_gbs
   cpu_baseline  the CPU oracle (numpy restatement of the reference path) on a bounded sample
@@ -64,6 +63,8 @@ def parse():
     ap.add_argument("--no-hbm", action="store_true", help="skip the HBM-resident secondary figure")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
     ap.add_argument("--cpu-heads", type=int, default=2, help="KV heads of one layer in the CPU sample")
+    ap.add_argument("--part", choices=["all", "host", "hbm", "config3"], default="all",
+                    help="profiling runs: only the host-resident step (host) or only the HBM-resident figure (hbm)")
     return ap.parse_args()
 
 
@@ -306,32 +307,41 @@ def config_dict(a, world):
 
 
 # ------------------------------------------------------------------ HBM-resident secondary figure
-def hbm_figure(a, dev, bp, off, peaks):
+HBM_SPECS = {
+    "config1": dict(hkv=8, g=4, n=131072, layers=36, k=512, batch=1,
+                    workload="config1: HBM-resident index + K/V, Qwen3-8B shape, T=131072, 36 layers, graph-captured step"),
+    "config3": dict(hkv=4, g=7, n=131072, layers=28, k=2048, batch=8,
+                    workload="config3: HBM-resident, Qwen2.5-7B shape (4 KV heads, G=7), 8 sequences x T=131072, "
+                             "28 layers, k=2048+4+64, graph-captured step"),
+}
+
+
+def hbm_figure(a, dev, bp, off, peaks, spec="config1"):
+    """A decode step with index and K/V rows in HBM (one CUDA graph per step), and the scan kernel's
+    mean duration from a graph of back-to-back scans."""
     from fathom_b200.synth import make_layer
-    n = a.hbm_ctx
+    sp = HBM_SPECS[spec]
+    n, BH, G, nl = sp["n"], sp["hkv"] * sp["batch"], sp["g"], sp["layers"]
+    if spec == "config1":
+        n = a.hbm_ctx
     layers, kvs = [], []
-    for L in range(a.layers):
-        d = make_layer(a.hkv, a.g, n, seed=1, layer=L, device=dev, kv_dtype=torch.bfloat16, with_v=True)
+    for L in range(nl):
+        d = make_layer(BH, G, n, seed=1 if spec == "config1" else 3, layer=L, device=dev, kv_dtype=torch.bfloat16,
+                       with_v=True)
         lay = Layer()
         lay.store = bp.PlaneStore(d["K"])
         lay.q, lay.g = d["q"], d["g"]
         lay.bytes = bp.bytes_planes(bp.make_plan(d["g"], a.budget)["t"], n)
         kvs.append((d["K"], d["V"]))
         layers.append(lay)
-    k_tot = a.k + a.sink + a.local
-    scores = torch.empty(a.hkv, a.g, n, device=dev)
+        del d
+    k_tot = sp["k"] + a.sink + a.local
+    scores = torch.empty(BH, G, n, device=dev)
 
-    def step(ev=None):
+    def step():
         for L, lay in enumerate(layers):
             plan = bp.make_plan(lay.g, a.budget)
-            if ev is not None:
-                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-                e1.record()    # creates the handle; the library records it again right after the scan kernel
-                e0.record()
-            idx = bp.scan_topk(lay.store, lay.q, plan, k_tot, a.sink, a.local, scores=scores,
-                               scan_done_event=e1 if ev is not None else None)
-            if ev is not None:
-                ev.append((e0, e1, lay.bytes))
+            idx = bp.scan_topk(lay.store, lay.q, plan, k_tot, a.sink, a.local, scores=scores)
             off.decode_attention(lay.q, idx, kvs[L][0], kvs[L][1], n)
 
     for _ in range(a.warmup):
@@ -342,6 +352,8 @@ def hbm_figure(a, dev, bp, off, peaks):
     with torch.cuda.graph(g):
         step()
     torch.cuda.synchronize()
+    for _ in range(a.warmup):
+        g.replay()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
     for _ in range(a.steps):
@@ -367,16 +379,16 @@ def hbm_figure(a, dev, bp, off, peaks):
     scan_ms = f0.elapsed_time(f1) / (a.steps * len(layers))
     byts = [lay.bytes for lay in layers]
     achieved = float(np.mean(byts)) / (scan_ms * 1e-3) / 1e9
-    del gs
-    rows = n * a.hkv * a.layers
-    del g
-    return {"workload": "config1: HBM-resident index + K/V, T=131072, 36 layers, graph-captured step",
+    rows = n * BH * nl
+    del g, gs, layers, kvs
+    torch.cuda.empty_cache()
+    return {"workload": sp["workload"],
             "value": rows / (ms * 1e-3), "unit": "key-rows/s", "ms_per_step": ms,
-            "scan_ms_per_layer": scan_ms, "scan_timing": "36 scan launches in one CUDA graph, mean per launch",
+            "scan_ms_per_layer": scan_ms, "scan_timing": f"{nl} scan launches in one CUDA graph, mean per launch",
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
                          "frac": achieved / peaks["hbm_gbs"], "traffic": None,
                          "bytes_per_launch": float(np.mean(byts))},
-            "bits_per_row": float(np.mean(byts)) * 8 / (n * a.hkv)}
+            "bits_per_row": float(np.mean(byts)) * 8 / (n * BH)}
 
 
 # ------------------------------------------------------------------ main
@@ -398,6 +410,14 @@ def main():
     from fathom_b200 import _lib
     _lib.lib()
     peaks, peaks_kind = measured_peaks()
+    if a.part == "hbm":
+        if rank == 0:
+            print(json.dumps({"hbm_resident": hbm_figure(a, dev, bp, off, peaks)}), flush=True)
+        return
+    if a.part == "config3":
+        if rank == 0:
+            print(json.dumps({"batched_hbm": hbm_figure(a, dev, bp, off, peaks, "config3")}), flush=True)
+        return
 
     link = host_link_gbs(dev)
     log(f"[rank {rank}] host link H2D {link:.1f} GB/s")
@@ -482,11 +502,12 @@ def main():
                     "d2h_bytes_per_step": out_host.numel() * 4},
             "gpu_launches": launches_per_layer * a.layers * a.steps,
             "clocks": clk, "peaks_source": peaks_kind}
-    if rank == 0 and world == 1 and not a.no_hbm:
+    if rank == 0 and world == 1 and not a.no_hbm and a.part == "all":
         del layers, kv
         torch.cuda.empty_cache()
         line["hbm_resident"] = hbm_figure(a, dev, bp, off, peaks)
-    if rank == 0 and world == 1 and not a.no_cpu:
+        line["batched_hbm"] = hbm_figure(a, dev, bp, off, peaks, "config3")
+    if rank == 0 and world == 1 and not a.no_cpu and a.part == "all":
         t, r = cpu_sample(a, a.cpu_heads)
         line["cpu_baseline"] = {"value": r / t, "unit": "key-rows/s", "cores": os.cpu_count(), "kind": "port",
                                 "sample": f"{a.cpu_heads} KV heads x {a.ctx} tokens of one layer: plan+scan+"

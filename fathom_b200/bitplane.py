@@ -275,13 +275,12 @@ def merge_topk(cand_scores, cand_idx, kk):
     return idx.view(*lead, kk), vals.view(*lead, kk)
 
 
-# ------------------------------------------------------------------ fused scan + selection
+# ------------------------------------------------------------------ scan + selection in one call
 def scan_select(store, q, plan, kk, mask_lo=0, mask_hi=None, index_offset=0, append_sink=0, append_local=0,
                 scores=None, with_scores=False, scan_done_event=None):
-    """store.scan(q, plan) and the top-kk selection of its rows in one fused pass (the selection
-    histogram is built in the scan epilogue).  Returns (idx int64 [BH, G, kk+append_sink+append_local],
-    vals fp32 [BH, G, kk] or None, scores fp32 [BH, G, n]).  scan_done_event (torch.cuda.Event) is
-    recorded right after the scan kernel."""
+    """store.scan(q, plan) and the top-kk selection of its rows in one library call.  Returns
+    (idx int64 [BH, G, kk+append_sink+append_local], vals fp32 [BH, G, kk] or None, scores fp32 [BH, G, n]).
+    scan_done_event (torch.cuda.Event) is recorded right after the scan kernel."""
     require_cuda(q)
     BH, G, d = q.shape
     assert BH == store.BH
@@ -306,7 +305,7 @@ def scan_select(store, q, plan, kk, mask_lo=0, mask_hi=None, index_offset=0, app
 
 
 def scan_topk(store, q, plan, k, sink=4, local=32, scores=None, scan_done_event=None):
-    """sink_local_topk(store.scan(q, plan), k, sink, local) in one fused pass; int64 [BH, G, k]."""
+    """sink_local_topk(store.scan(q, plan), k, sink, local) in one call; int64 [BH, G, k]."""
     idx, _, _ = scan_select(store, q, plan, k - sink - local, mask_lo=sink, mask_hi=store.n - local,
                             append_sink=sink, append_local=local, scores=scores, scan_done_event=scan_done_event)
     return idx

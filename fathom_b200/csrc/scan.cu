@@ -65,29 +65,20 @@ __device__ __forceinline__ void tokens(float (&acc)[G][TPL], const uint32_t (&w)
   }
 }
 
-// Selection histogram fused into the scan epilogue (HIST = true): the same 4096-bin histogram of the
-// top 12 key bits that the selection's hist pass builds, for tokens in [mask_lo, mask_hi).
-struct HistArgs {
-  int64_t mask_lo, mask_hi, kk;
-  uint32_t* hist;    // [BH*G][4096]
-  uint32_t* ticket;  // [BH] CTAs finished per (batch, kv-head) row
-  uint32_t* bstar;   // [BH*G] boundary bins
-};
-
 template <int TPL, int G>
 constexpr int min_blocks() { return TPL == 32 ? 2 : TPL == 16 ? (G > 4 ? 2 : 3) : (G > 4 ? 3 : 5); }
 
-template <int G, int TPL, bool HIST>
+template <int G, int TPL>
 __global__ void __launch_bounds__(WARPS * 32, (min_blocks<TPL, G>()))
     scan_kernel(const float* __restrict__ q, const int32_t* __restrict__ cls, const int32_t* __restrict__ clsn,
                 int bmax, const uint32_t* __restrict__ planes32, const uint16_t* __restrict__ scales, int64_t n,
                 int64_t nblk, int64_t nsb, int64_t sub, int64_t blk_begin, int64_t blk_end, int64_t grp_begin,
-                float* __restrict__ out, HistArgs ha) {
+                float* __restrict__ out) {
   constexpr int LPW = 32 / TPL;          // lanes sharing a plane half-word
   constexpr int NHW = 32 / LPW;          // half-words per warp
   constexpr int BPW = NHW / 2;           // blocks per warp
   constexpr int STAGE_U32 = stage_u32<TPL>();
-  extern __shared__ uint32_t s_stage[];  // [WARPS][2][STAGE_U32], then (HIST) [G][NBINS/2] packed u16 counters
+  extern __shared__ uint32_t s_stage[];  // [WARPS][2][STAGE_U32]
   __shared__ float s_q[G][D];
   __shared__ int s_ch[D], s_t[D], s_slot[D];
   __shared__ int s_bstart[MAXB + 1];
@@ -95,9 +86,6 @@ __global__ void __launch_bounds__(WARPS * 32, (min_blocks<TPL, G>()))
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int64_t bh = blockIdx.y;
-  uint32_t* s_hist = s_stage + WARPS * 2 * STAGE_U32;
-  if (HIST)
-    for (int e = tid; e < G * selectk::NBINS / 2; e += blockDim.x) s_hist[e] = 0;
   for (int e = tid; e < G * D; e += blockDim.x) s_q[e / D][e % D] = q[bh * G * D + e];
   // one round of global loads: the query tile above, and here every thread's column of the four
   // class lists plus the class counts; then the flat channel list in class order (depth 1, 2, 3, 4).
@@ -238,94 +226,62 @@ __global__ void __launch_bounds__(WARPS * 32, (min_blocks<TPL, G>()))
       }
     }
   }
-  const int64_t tok0 = blk * BLK + half * 32 + bitoff;
-  if (active) {
-    const bool full = tok0 + TPL <= n;
-    const bool vec = full && (n % 4 == 0) && ((reinterpret_cast<uintptr_t>(out) & 15) == 0);
+  // Epilogue, one query head at a time: the warp's scores go through its (now idle) staging area, so
+  // the global stores are fully coalesced (512 contiguous bytes per warp instruction).
+  // Lane l owns warp tokens l*TPL .. l*TPL+TPL-1; float4 slot j of lane l's row is stored at
+  // j ^ swz(l), which keeps both the row writes and the token-order reads free of bank conflicts.
+  constexpr int R = TPL / 4;                       // float4 per lane row
+  constexpr int ROWS_PER_128B = 8 / R;
+  float* s_sc = reinterpret_cast<float*>(stage);   // 32 * TPL floats
+  const int64_t wtok0 = wblk0 * BLK;               // first token of the warp
+  const int64_t tok_lo = (warp_live ? lo : 0) * BLK;
+  const int64_t tok_hi = warp_live ? (hi_lim * BLK < n ? hi_lim * BLK : n) : 0;   // valid tokens: [tok_lo, tok_hi)
+  auto swz = [](int row) { return (row / ROWS_PER_128B) & (R - 1); };
+  const bool vec_ok = (n % 4 == 0) && ((reinterpret_cast<uintptr_t>(out) & 15) == 0);
 #pragma unroll
-    for (int g = 0; g < G; ++g) {
-      float* o = out + (bh * G + g) * n + tok0;
-      if (vec) {
+  for (int g = 0; g < G; ++g) {
+    __syncwarp();
 #pragma unroll
-        for (int k = 0; k < TPL; k += 4)
-          *reinterpret_cast<float4*>(o + k) = make_float4(acc[g][k] + cst[g], acc[g][k + 1] + cst[g],
-                                                          acc[g][k + 2] + cst[g], acc[g][k + 3] + cst[g]);
-      } else {
+    for (int j = 0; j < R; ++j)
+      reinterpret_cast<float4*>(s_sc)[lane * R + (j ^ swz(lane))] =
+          make_float4(acc[g][4 * j] + cst[g], acc[g][4 * j + 1] + cst[g], acc[g][4 * j + 2] + cst[g],
+                      acc[g][4 * j + 3] + cst[g]);
+    __syncwarp();
+    if (warp_live) {
+      float* o = out + (bh * G + g) * n;
+      // coalesced stores: iteration it covers warp tokens it*128 .. it*128+127, 4 per lane
+#pragma unroll 1
+      for (int it = 0; it < TPL / 4; ++it) {
+        const int t = it * 128 + 4 * lane;
+        const int row = t / TPL, j = (t % TPL) / 4;
+        const float4 v = reinterpret_cast<const float4*>(s_sc)[row * R + (j ^ swz(row))];
+        const int64_t tg = wtok0 + t;
+        if (vec_ok && tg >= tok_lo && tg + 4 <= tok_hi) {
+          *reinterpret_cast<float4*>(o + tg) = v;
+        } else {
+          const float e[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
-        for (int k = 0; k < TPL; ++k)
-          if (tok0 + k < n) o[k] = acc[g][k] + cst[g];
-      }
-    }
-  }
-  if (HIST) {
-    if (active) {
-      // this lane's tokens, as a bit mask of the ones that are counted unmasked (the rest count as -inf)
-      const bool plain = tok0 >= ha.mask_lo && tok0 + TPL <= ha.mask_hi && tok0 + TPL <= n;
-#pragma unroll
-      for (int g = 0; g < G; ++g) {
-#pragma unroll
-        for (int k = 0; k < TPL; ++k) {
-          const int64_t tok = tok0 + k;
-          if (plain || tok < n) {
-            const bool in = plain || (tok >= ha.mask_lo && tok < ha.mask_hi);
-            const uint32_t key = in ? f2key(acc[g][k] + cst[g]) : KEY_NEG_INF;
-            const uint32_t bin = key >> (32 - selectk::HBITS);
-            atomicAdd(&s_hist[g * (selectk::NBINS / 2) + (bin >> 1)], 1u << ((bin & 1) * 16));
-          }
+          for (int u = 0; u < 4; ++u)
+            if (tg + u >= tok_lo && tg + u < tok_hi) o[tg + u] = e[u];
         }
-      }
-    }
-    __syncthreads();
-    for (int e = tid; e < G * selectk::NBINS / 2; e += blockDim.x) {
-      const uint32_t v = s_hist[e];
-      if (v) {
-        const int g = e / (selectk::NBINS / 2), b2 = (e % (selectk::NBINS / 2)) * 2;
-        uint32_t* gh = ha.hist + (bh * G + g) * selectk::NBINS + b2;
-        if (v & 0xFFFFu) atomicAdd(gh, v & 0xFFFFu);
-        if (v >> 16) atomicAdd(gh + 1, v >> 16);
-      }
-    }
-    // the last CTA of this (batch, kv-head) row derives the G boundary bins (no CTA waits)
-    __shared__ bool s_last;
-    __shared__ uint32_t s_part[WARPS * 32];
-    __shared__ int s_res;
-    __threadfence();
-    __syncthreads();
-    if (tid == 0) s_last = atomicAdd(&ha.ticket[bh], 1u) == gridDim.x - 1;
-    __syncthreads();
-    if (s_last) {
-      __threadfence();
-      uint32_t* s_row = s_stage;  // the staging buffers are free now
-      for (int g = 0; g < G; ++g) {
-        const uint32_t* gh = ha.hist + (bh * G + g) * selectk::NBINS;
-        for (int b = tid; b < selectk::NBINS; b += blockDim.x) s_row[b] = __ldcg(&gh[b]);
-        __syncthreads();
-        const int bs = selectk::boundary_bin(s_row, ha.kk, s_part, &s_res);
-        if (tid == 0) ha.bstar[bh * G + g] = (uint32_t)bs;
-        __syncthreads();
       }
     }
   }
 }
 
-template <int G, int TPL, bool HIST>
+template <int G, int TPL>
 int launch_scan(const float* q, int64_t BH, int64_t n, int64_t nblk, int64_t nsb, int64_t sub, const int32_t* cls,
                 const int32_t* clsn, int bmax, const uint32_t* planes32, const uint16_t* scales, int64_t b0, int64_t b1,
-                float* out, const HistArgs& ha, cudaStream_t st) {
+                float* out, cudaStream_t st) {
   constexpr int BPW = TPL / 2;
   const int64_t g0 = b0 / BPW, g1 = cdiv(b1, BPW);
   const int64_t grid_x = cdiv(g1 - g0, WARPS);
   FATHOM_REQUIRE(grid_x <= 0x7fffffffLL && BH <= 65535, FATHOM_ERR_SHAPE, "scan: grid too large");
-  size_t smem = (size_t)WARPS * 2 * stage_u32<TPL>() * sizeof(uint32_t);
-  if (HIST) {  // the histogram follows the staging area, and the last CTA reuses staging for one row
-    smem += (size_t)G * selectk::NBINS / 2 * sizeof(uint32_t);
-    const size_t row_bytes = selectk::NBINS * sizeof(uint32_t);
-    if (smem < row_bytes) smem = row_bytes;
-  }
-  cudaFuncSetAttribute(scan_kernel<G, TPL, HIST>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  const size_t smem = (size_t)WARPS * 2 * stage_u32<TPL>() * sizeof(uint32_t);
+  cudaFuncSetAttribute(scan_kernel<G, TPL>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   dim3 grid((unsigned)grid_x, (unsigned)BH);
-  scan_kernel<G, TPL, HIST><<<grid, WARPS * 32, smem, st>>>(q, cls, clsn, bmax, planes32, scales, n, nblk, nsb, sub,
-                                                            b0, b1, g0, out, ha);
+  scan_kernel<G, TPL><<<grid, WARPS * 32, smem, st>>>(q, cls, clsn, bmax, planes32, scales, n, nblk, nsb, sub, b0, b1,
+                                                      g0, out);
   return check_launch("scan");
 }
 
@@ -350,7 +306,7 @@ int sm_count() {
 
 int scan_dispatch(const float* q, int64_t BH, int G, int64_t n, int64_t sub, const int32_t* cls, const int32_t* clsn,
                   int bmax, const uint64_t* planes_k, const uint16_t* scales_k, int64_t blk_begin, int64_t blk_end,
-                  float* scores, const HistArgs* ha, cudaStream_t st) {
+                  float* scores, cudaStream_t st) {
   FATHOM_REQUIRE(q && cls && clsn && planes_k && scales_k && scores, FATHOM_ERR_NULL, "scan: NULL pointer");
   FATHOM_REQUIRE(BH >= 1 && BH <= 65535 && n >= 1 && sub >= 1, FATHOM_ERR_SHAPE, "scan: bad shape (BH=%lld n=%lld)",
                  (long long)BH, (long long)n);
@@ -364,7 +320,6 @@ int scan_dispatch(const float* q, int64_t BH, int G, int64_t n, int64_t sub, con
                  (long long)nblk);
   if (blk_begin == blk_end) return FATHOM_OK;
   const uint32_t* p32 = reinterpret_cast<const uint32_t*>(planes_k);
-  HistArgs none{};
   // tokens per lane: 32 for G <= 4 (16 for G > 4, to bound registers); a split 4x finer only when the
   // coarse one would leave most SMs without a warp
   const int64_t range = blk_end - blk_begin;
@@ -375,11 +330,8 @@ int scan_dispatch(const float* q, int64_t BH, int G, int64_t n, int64_t sub, con
     const int v = atoi(env);
     if (v == 8 || v == 16 || (v == 32 && G <= 4)) tpl = v;
   }
-#define FATHOM_SCAN_LAUNCH(GG, TT)                                                                                  \
-  return ha ? launch_scan<GG, TT, true>(q, BH, n, nblk, nsb, sub, cls, clsn, bmax, p32, scales_k, blk_begin,        \
-                                        blk_end, scores, *ha, st)                                                   \
-            : launch_scan<GG, TT, false>(q, BH, n, nblk, nsb, sub, cls, clsn, bmax, p32, scales_k, blk_begin,       \
-                                         blk_end, scores, none, st);
+#define FATHOM_SCAN_LAUNCH(GG, TT) \
+  return launch_scan<GG, TT>(q, BH, n, nblk, nsb, sub, cls, clsn, bmax, p32, scales_k, blk_begin, blk_end, scores, st);
 #define FATHOM_SCAN_CASE4(GG)                    \
   case GG:                                       \
     if (tpl == 32) { FATHOM_SCAN_LAUNCH(GG, 32) } \
@@ -410,7 +362,7 @@ int scan_dispatch(const float* q, int64_t BH, int G, int64_t n, int64_t sub, con
 extern "C" int fathom_scan(const float* q, int64_t BH, int G, int64_t n, int64_t sub, const int32_t* cls,
                            const int32_t* clsn, int bmax, const uint64_t* planes_k, const uint16_t* scales_k,
                            int64_t blk_begin, int64_t blk_end, float* scores, void* stream) {
-  return scan_dispatch(q, BH, G, n, sub, cls, clsn, bmax, planes_k, scales_k, blk_begin, blk_end, scores, nullptr,
+  return scan_dispatch(q, BH, G, n, sub, cls, clsn, bmax, planes_k, scales_k, blk_begin, blk_end, scores,
                        reinterpret_cast<cudaStream_t>(stream));
 }
 
@@ -436,17 +388,13 @@ extern "C" int fathom_scan_select(const float* q, int64_t BH, int G, int64_t n, 
                  FATHOM_ERR_WORKSPACE, "scan_select: workspace needs %zu bytes, 256-byte aligned",
                  selectk::ws_bytes(rows));
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-  selectk::Workspace w = selectk::carve(workspace, rows);
-  cudaError_t e = cudaMemsetAsync(workspace, 0, selectk::zeroed_bytes(rows), st);
-  if (e != cudaSuccess) return set_error(FATHOM_ERR_CUDA, "scan_select: memset: %s", cudaGetErrorString(e));
-  HistArgs ha{mask_lo, mask_hi, kk, w.hist, w.ticket, w.bstar};
   const int64_t nblk = cdiv(n, BLK);
-  int r = scan_dispatch(q, BH, G, n, sub, cls, clsn, bmax, planes_k, scales_k, 0, nblk, scores, &ha, st);
+  int r = scan_dispatch(q, BH, G, n, sub, cls, clsn, bmax, planes_k, scales_k, 0, nblk, scores, st);
   if (r != FATHOM_OK) return r;
   if (scan_done_event) {
-    e = cudaEventRecord(reinterpret_cast<cudaEvent_t>(scan_done_event), st);
+    const cudaError_t e = cudaEventRecord(reinterpret_cast<cudaEvent_t>(scan_done_event), st);
     if (e != cudaSuccess) return set_error(FATHOM_ERR_CUDA, "scan_select: event record: %s", cudaGetErrorString(e));
   }
-  return selectk::launch_select_tail(scores, rows, n, n, kk, mask_lo, mask_hi, index_offset, out_idx, out_stride,
-                                     out_scores, append_sink, append_local, w, st);
+  return selectk::launch_select(scores, rows, n, n, kk, mask_lo, mask_hi, index_offset, out_idx, out_stride,
+                                out_scores, append_sink, append_local, workspace, workspace_bytes, st);
 }

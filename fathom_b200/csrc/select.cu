@@ -52,8 +52,6 @@ __global__ void __launch_bounds__(HT) hist_kernel(const float* __restrict__ scor
                                                   uint32_t* __restrict__ ghist, uint32_t* __restrict__ ticket,
                                                   uint32_t* __restrict__ bstar) {
   __shared__ uint32_t sh[NBINS];
-  __shared__ uint32_t s_part[HT];
-  __shared__ int s_res;
   __shared__ bool s_last;
   const int64_t row = blockIdx.y;
   for (int b = threadIdx.x; b < NBINS; b += HT) sh[b] = 0;
@@ -75,11 +73,9 @@ __global__ void __launch_bounds__(HT) hist_kernel(const float* __restrict__ scor
   __syncthreads();
   if (threadIdx.x == 0) s_last = atomicAdd(&ticket[row], 1u) == gridDim.x - 1;
   __syncthreads();
-  if (!s_last) return;
+  if (!s_last || threadIdx.x >= 32) return;
   __threadfence();
-  for (int b = threadIdx.x; b < NBINS; b += HT) sh[b] = __ldcg(&gh[b]);
-  __syncthreads();
-  const int bs = boundary_bin(sh, kk, s_part, &s_res);
+  const int bs = warp_boundary_bin(gh, kk);
   if (threadIdx.x == 0) bstar[row] = (uint32_t)bs;
 }
 
@@ -220,35 +216,73 @@ __device__ void exact_select_row(const float* r, int64_t n, int64_t kk, int64_t 
 // Radix select on 64-bit candidates held in shared memory: returns (to every thread) the
 // smallest value C such that exactly kk of the n values are >= C.  The values are unique; the
 // top 12 bits of the kk-th largest are `top12` and `need` of the values equal it in those bits.
+// Per level one pass counts the values still matching the prefix and histograms their next digit;
+// one warp then finds the digit.  It stops as soon as the prefix holds exactly `need` values.
 __device__ uint64_t refine_threshold(const uint64_t* s_v, int n, uint32_t top12, int64_t need, uint32_t* s_hist,
-                                     uint32_t* s_part, int* s_res, uint32_t* s_warp) {
+                                     uint32_t* s_ctl) {
   uint64_t prefix = (uint64_t)top12 << 52;
   uint64_t pmask = 0xFFFull << 52;
   const int shifts[5] = {40, 28, 16, 4, 0};
   const int widths[5] = {12, 12, 12, 12, 4};
   for (int lv = 0; lv < 5; ++lv) {
-    // values still matching the prefix
-    uint32_t cnt = 0;
-    for (int i = threadIdx.x; i < n; i += blockDim.x) cnt += (s_v[i] & pmask) == prefix;
-    uint32_t tot;
-    block_exclusive_scan(cnt, s_warp, &tot);
-    if ((int64_t)tot == need) break;
     const int sh = shifts[lv], nb = 1 << widths[lv];
     for (int b = threadIdx.x; b < NBINS; b += blockDim.x) s_hist[b] = 0;
+    if (threadIdx.x == 0) s_ctl[0] = 0;
     __syncthreads();
-    for (int i = threadIdx.x; i < n; i += blockDim.x)
-      if ((s_v[i] & pmask) == prefix) atomicAdd(&s_hist[(s_v[i] >> sh) & (nb - 1)], 1u);
+    uint32_t match = 0;
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+      const uint64_t v = s_v[i];
+      if ((v & pmask) == prefix) {
+        ++match;
+        atomicAdd(&s_hist[(v >> sh) & (nb - 1)], 1u);
+      }
+    }
+    match += __shfl_xor_sync(0xffffffffu, match, 16);
+    match += __shfl_xor_sync(0xffffffffu, match, 8);
+    match += __shfl_xor_sync(0xffffffffu, match, 4);
+    match += __shfl_xor_sync(0xffffffffu, match, 2);
+    match += __shfl_xor_sync(0xffffffffu, match, 1);
+    if ((threadIdx.x & 31) == 0 && match) atomicAdd(&s_ctl[0], match);
     __syncthreads();
-    const int b = boundary_bin(s_hist, need, s_part, s_res);
-    uint32_t above = 0;
-    for (int x = threadIdx.x; x < NBINS; x += blockDim.x)
-      if (x > b) above += s_hist[x];
-    block_exclusive_scan(above, s_warp, &tot);
-    need -= tot;
-    prefix |= (uint64_t)b << sh;
+    if ((int64_t)s_ctl[0] == need) break;  // uniform: every value matching the prefix is taken
+    if (threadIdx.x < 32) {
+      uint32_t above;
+      const int b = warp_boundary_bin_smem(s_hist, need, &above);
+      if (threadIdx.x == 0) {
+        s_ctl[1] = (uint32_t)b;
+        s_ctl[2] = above;
+      }
+    }
+    __syncthreads();
+    need -= s_ctl[2];
+    prefix |= (uint64_t)s_ctl[1] << sh;
     pmask |= (uint64_t)(nb - 1) << sh;
+    __syncthreads();  // s_ctl is rewritten by the next level
   }
   return prefix;
+}
+
+// Descending bitonic sort of P (power of two, <= blockDim.x) values, one per thread: v of thread i is
+// element i.  Partners closer than a warp are exchanged with shuffles, farther ones through shared
+// memory (s_x, P entries).  Returns this thread's element of the sorted order.
+__device__ uint64_t bitonic_desc_regs(uint64_t v, int P, uint64_t* s_x) {
+  const int i = threadIdx.x;
+  for (int k = 2; k <= P; k <<= 1) {
+    for (int j = k >> 1; j > 0; j >>= 1) {
+      uint64_t other;
+      if (j >= 32) {
+        if (i < P) s_x[i] = v;
+        __syncthreads();
+        other = i < P ? s_x[i ^ j] : v;
+        __syncthreads();
+      } else {
+        other = __shfl_xor_sync(0xffffffffu, v, j);
+      }
+      const bool keep_max = ((i & k) == 0) == ((i & j) == 0);
+      if (i < P) v = keep_max ? (v > other ? v : other) : (v < other ? v : other);
+    }
+  }
+  return v;
 }
 
 __global__ void __launch_bounds__(FT) finalize_kernel(const float* __restrict__ scores, int64_t n, int64_t row_stride,
@@ -265,6 +299,7 @@ __global__ void __launch_bounds__(FT) finalize_kernel(const float* __restrict__ 
   __shared__ uint32_t s_hist[NBINS];
   __shared__ uint32_t s_part[FT];
   __shared__ uint32_t s_warp[33];
+  __shared__ uint32_t s_ctl[4];
   __shared__ uint32_t s_cnt;
   __shared__ int s_res;
   const int64_t row = blockIdx.x;
@@ -277,27 +312,50 @@ __global__ void __launch_bounds__(FT) finalize_kernel(const float* __restrict__ 
       s_buf[i] = v;
       above += (uint32_t)(v >> 52) > top12;
     }
-    uint32_t tot;
-    block_exclusive_scan(above, s_warp, &tot);  // also orders the loads above before the reads below
-    const uint64_t C = refine_threshold(s_buf, (int)cnt, top12, kk - (int64_t)tot, s_hist, s_part, &s_res, s_warp);
+    above += __shfl_xor_sync(0xffffffffu, above, 16);
+    above += __shfl_xor_sync(0xffffffffu, above, 8);
+    above += __shfl_xor_sync(0xffffffffu, above, 4);
+    above += __shfl_xor_sync(0xffffffffu, above, 2);
+    above += __shfl_xor_sync(0xffffffffu, above, 1);
+    if (threadIdx.x == 0) s_cnt = 0;
+    __syncthreads();
+    if ((threadIdx.x & 31) == 0 && above) atomicAdd(&s_cnt, above);
+    __syncthreads();
+    const uint32_t tot = s_cnt;
+    __syncthreads();
+    const uint64_t C = refine_threshold(s_buf, (int)cnt, top12, kk - (int64_t)tot, s_hist, s_ctl);
     if (threadIdx.x == 0) s_cnt = 0;
     __syncthreads();
     for (int i = threadIdx.x; i < (int)cnt; i += blockDim.x)
-      if (s_buf[i] >= C) s_sel[atomicAdd(&s_cnt, 1u)] = s_buf[i];
+      if (s_buf[i] >= C) {
+        const uint32_t pos = atomicAdd(&s_cnt, 1u);
+        if (pos < (uint32_t)MAX_KK) s_sel[pos] = s_buf[i];
+      }
     __syncthreads();
   } else {
     exact_select_row(scores + row * row_stride, n, kk, mask_lo, mask_hi, s_sel, s_hist, s_part, &s_res, s_warp,
                      &s_cnt);
   }
   const int P = next_pow2((int)kk);
-  for (int i = (int)kk + threadIdx.x; i < P; i += blockDim.x) s_sel[i] = 0ull;
-  __syncthreads();
-  bitonic_desc(s_sel, P);
   int64_t* o = out_idx + row * out_stride;
-  for (int i = threadIdx.x; i < kk; i += blockDim.x) {
-    const uint64_t v = s_sel[i];
-    o[i] = (int64_t)(uint32_t)(~(uint32_t)v) + index_offset;
-    if (out_scores) out_scores[row * kk + i] = key2f((uint32_t)(v >> 32));
+  if (P <= FT) {
+    // one value per thread, sorted in registers
+    uint64_t v = threadIdx.x < kk ? s_sel[threadIdx.x] : 0ull;
+    __syncthreads();
+    v = bitonic_desc_regs(v, P, s_buf);
+    if (threadIdx.x < kk) {
+      o[threadIdx.x] = (int64_t)(uint32_t)(~(uint32_t)v) + index_offset;
+      if (out_scores) out_scores[row * kk + threadIdx.x] = key2f((uint32_t)(v >> 32));
+    }
+  } else {
+    for (int i = (int)kk + threadIdx.x; i < P; i += blockDim.x) s_sel[i] = 0ull;
+    __syncthreads();
+    bitonic_desc(s_sel, P);
+    for (int i = threadIdx.x; i < kk; i += blockDim.x) {
+      const uint64_t v = s_sel[i];
+      o[i] = (int64_t)(uint32_t)(~(uint32_t)v) + index_offset;
+      if (out_scores) out_scores[row * kk + i] = key2f((uint32_t)(v >> 32));
+    }
   }
   for (int64_t i = threadIdx.x; i < append_sink; i += blockDim.x) o[kk + i] = i;
   for (int64_t i = threadIdx.x; i < append_local; i += blockDim.x) o[kk + append_sink + i] = n - append_local + i;
@@ -306,18 +364,77 @@ __global__ void __launch_bounds__(FT) finalize_kernel(const float* __restrict__ 
 __global__ void __launch_bounds__(FT) merge_kernel(const float* __restrict__ cs, const int64_t* __restrict__ ci,
                                                    int64_t m, int64_t kk, int64_t* __restrict__ out_idx,
                                                    float* __restrict__ out_scores) {
-  extern __shared__ uint64_t s_buf[];
+  extern __shared__ uint64_t s_dyn[];  // CAP candidates, then MAX_KK selected
+  uint64_t* s_buf = s_dyn;
+  uint64_t* s_sel = s_dyn + CAP;
+  __shared__ uint32_t s_hist[NBINS];
+  __shared__ uint32_t s_ctl[4];
+  __shared__ uint32_t s_cnt;
   const int64_t row = blockIdx.x;
-  const int P = next_pow2((int)m);
-  for (int i = threadIdx.x; i < P; i += blockDim.x)
-    s_buf[i] = i < m ? ((uint64_t)f2key(cs[row * m + i]) << 32) | (uint32_t)(~(uint32_t)ci[row * m + i]) : 0ull;
+  for (int b = threadIdx.x; b < NBINS; b += blockDim.x) s_hist[b] = 0;
   __syncthreads();
-  bitonic_desc(s_buf, P);
-  for (int i = threadIdx.x; i < kk; i += blockDim.x) {
-    const uint64_t v = s_buf[i];
-    out_idx[row * kk + i] = (int64_t)(uint32_t)(~(uint32_t)v);
-    if (out_scores) out_scores[row * kk + i] = key2f((uint32_t)(v >> 32));
+  for (int i = threadIdx.x; i < m; i += blockDim.x) {
+    const uint64_t v = ((uint64_t)f2key(cs[row * m + i]) << 32) | (uint32_t)(~(uint32_t)ci[row * m + i]);
+    s_buf[i] = v;
+    atomicAdd(&s_hist[v >> 52], 1u);
   }
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    uint32_t above;
+    const int b = warp_boundary_bin_smem(s_hist, kk, &above);
+    if (threadIdx.x == 0) {
+      s_ctl[1] = (uint32_t)b;
+      s_ctl[2] = above;
+    }
+  }
+  __syncthreads();
+  const uint32_t top12 = s_ctl[1];
+  const int64_t need = kk - (int64_t)s_ctl[2];
+  __syncthreads();
+  const uint64_t C = refine_threshold(s_buf, (int)m, top12, need, s_hist, s_ctl);
+  if (threadIdx.x == 0) s_cnt = 0;
+  __syncthreads();
+  for (int i = threadIdx.x; i < m; i += blockDim.x)
+    if (s_buf[i] >= C) {
+      const uint32_t pos = atomicAdd(&s_cnt, 1u);
+      if (pos < (uint32_t)MAX_KK) s_sel[pos] = s_buf[i];   // distinct indices give exactly kk
+    }
+  __syncthreads();
+  const int P = next_pow2((int)kk);
+  if (P <= FT) {
+    uint64_t v = threadIdx.x < kk ? s_sel[threadIdx.x] : 0ull;
+    __syncthreads();
+    v = bitonic_desc_regs(v, P, s_buf);
+    if (threadIdx.x < kk) {
+      out_idx[row * kk + threadIdx.x] = (int64_t)(uint32_t)(~(uint32_t)v);
+      if (out_scores) out_scores[row * kk + threadIdx.x] = key2f((uint32_t)(v >> 32));
+    }
+  } else {
+    for (int i = (int)kk + threadIdx.x; i < P; i += blockDim.x) s_sel[i] = 0ull;
+    __syncthreads();
+    bitonic_desc(s_sel, P);
+    for (int i = threadIdx.x; i < kk; i += blockDim.x) {
+      const uint64_t v = s_sel[i];
+      out_idx[row * kk + i] = (int64_t)(uint32_t)(~(uint32_t)v);
+      if (out_scores) out_scores[row * kk + i] = key2f((uint32_t)(v >> 32));
+    }
+  }
+}
+
+// collect + finalize on a histogram and boundary bins already built
+int select_tail(const float* scores, int64_t rows, int64_t n, int64_t row_stride, int64_t kk, int64_t mask_lo,
+                       int64_t mask_hi, int64_t index_offset, int64_t* out_idx, int64_t out_stride,
+                       float* out_scores, int64_t append_sink, int64_t append_local, const Workspace& w,
+                       cudaStream_t st) {
+  const int64_t chunks = cdiv(n, CHUNK);
+  dim3 grid((unsigned)chunks, (unsigned)rows);
+  collect_kernel<<<grid, HT, 0, st>>>(scores, n, row_stride, mask_lo, mask_hi, w.bstar, w.count, w.cand);
+  const size_t smem = (CAP + MAX_KK) * sizeof(uint64_t);
+  cudaFuncSetAttribute(finalize_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  finalize_kernel<<<(unsigned)rows, FT, smem, st>>>(scores, n, row_stride, kk, mask_lo, mask_hi, w.count, w.bstar,
+                                                     w.cand, index_offset, out_idx, out_stride, out_scores,
+                                                     append_sink, append_local);
+  return check_launch("select_topk");
 }
 
 int run_select(const float* scores, int64_t rows, int64_t n, int64_t row_stride, int64_t kk, int64_t mask_lo,
@@ -340,27 +457,21 @@ int run_select(const float* scores, int64_t rows, int64_t n, int64_t row_stride,
   const int64_t chunks = cdiv(n, CHUNK);
   dim3 grid((unsigned)chunks, (unsigned)rows);
   hist_kernel<<<grid, HT, 0, st>>>(scores, n, row_stride, kk, mask_lo, mask_hi, w.hist, w.ticket, w.bstar);
-  return launch_select_tail(scores, rows, n, row_stride, kk, mask_lo, mask_hi, index_offset, out_idx, out_stride,
+  return select_tail(scores, rows, n, row_stride, kk, mask_lo, mask_hi, index_offset, out_idx, out_stride,
                             out_scores, append_sink, append_local, w, st);
 }
 
 }  // namespace
 
 namespace selectk {
-int launch_select_tail(const float* scores, int64_t rows, int64_t n, int64_t row_stride, int64_t kk, int64_t mask_lo,
-                       int64_t mask_hi, int64_t index_offset, int64_t* out_idx, int64_t out_stride,
-                       float* out_scores, int64_t append_sink, int64_t append_local, const Workspace& w,
-                       cudaStream_t st) {
-  const int64_t chunks = cdiv(n, CHUNK);
-  dim3 grid((unsigned)chunks, (unsigned)rows);
-  collect_kernel<<<grid, HT, 0, st>>>(scores, n, row_stride, mask_lo, mask_hi, w.bstar, w.count, w.cand);
-  const size_t smem = (CAP + MAX_KK) * sizeof(uint64_t);
-  cudaFuncSetAttribute(finalize_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  finalize_kernel<<<(unsigned)rows, FT, smem, st>>>(scores, n, row_stride, kk, mask_lo, mask_hi, w.count, w.bstar,
-                                                     w.cand, index_offset, out_idx, out_stride, out_scores,
-                                                     append_sink, append_local);
-  return check_launch("select_topk");
+int launch_select(const float* scores, int64_t rows, int64_t n, int64_t row_stride, int64_t kk, int64_t mask_lo,
+                  int64_t mask_hi, int64_t index_offset, int64_t* out_idx, int64_t out_stride, float* out_scores,
+                  int64_t append_sink, int64_t append_local, void* workspace, size_t workspace_bytes,
+                  cudaStream_t st) {
+  return run_select(scores, rows, n, row_stride, kk, mask_lo, mask_hi, index_offset, out_idx, out_stride, out_scores,
+                    append_sink, append_local, workspace, workspace_bytes, st);
 }
+
 }  // namespace selectk
 }  // namespace fathom
 
@@ -394,9 +505,9 @@ extern "C" int fathom_sink_local_topk(const float* scores, int64_t rows, int64_t
 extern "C" int fathom_merge_topk(const float* cand_scores, const int64_t* cand_idx, int64_t rows, int64_t m, int64_t kk,
                                  int64_t* out_idx, float* out_scores, void* stream) {
   FATHOM_REQUIRE(cand_scores && cand_idx && out_idx, FATHOM_ERR_NULL, "merge_topk: NULL pointer");
-  FATHOM_REQUIRE(rows >= 1 && rows <= 0x7fffffffLL && m >= 1 && m <= CAP && kk >= 1 && kk <= m, FATHOM_ERR_SHAPE,
-                 "merge_topk: need 1 <= kk <= m <= %d", CAP);
-  const size_t smem = CAP * sizeof(uint64_t);
+  FATHOM_REQUIRE(rows >= 1 && rows <= 0x7fffffffLL && m >= 1 && m <= CAP && kk >= 1 && kk <= m && kk <= MAX_KK,
+                 FATHOM_ERR_SHAPE, "merge_topk: need 1 <= kk <= min(m, %d), m <= %d", MAX_KK, CAP);
+  const size_t smem = (CAP + MAX_KK) * sizeof(uint64_t);
   cudaFuncSetAttribute(merge_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   merge_kernel<<<(unsigned)rows, FT, smem, reinterpret_cast<cudaStream_t>(stream)>>>(cand_scores, cand_idx, m, kk,
                                                                                      out_idx, out_scores);

@@ -112,11 +112,82 @@ static __device__ uint32_t block_exclusive_scan(uint32_t v, uint32_t* s_warp, ui
 }
 
 
-// collect + finalize on a histogram (and boundary bins) already built: see select.cu.
-int launch_select_tail(const float* scores, int64_t rows, int64_t n, int64_t row_stride, int64_t kk, int64_t mask_lo,
-                       int64_t mask_hi, int64_t index_offset, int64_t* out_idx, int64_t out_stride,
-                       float* out_scores, int64_t append_sink, int64_t append_local, const Workspace& w,
-                       cudaStream_t st);
+// Boundary bin of one row histogram (NBINS counters in global memory, read through L2), found by one
+// warp: each lane sums 128 consecutive bins, a shuffle suffix-scan finds the lane holding the bin,
+// which walks its bins from the top.  Returns (to every lane) the largest bin b with
+// sum_{b' >= b} hist[b'] >= kk, or 0 if the row holds fewer than kk keys.
+static __device__ int warp_boundary_bin(const uint32_t* hist, int64_t kk) {
+  const int lane = threadIdx.x & 31;
+  constexpr int PER = NBINS / 32;
+  const uint4* h4 = reinterpret_cast<const uint4*>(hist + lane * PER);
+  uint32_t part = 0;
+#pragma unroll 8
+  for (int i = 0; i < PER / 4; ++i) {
+    const uint4 v = __ldcg(h4 + i);
+    part += v.x + v.y + v.z + v.w;
+  }
+  uint32_t suffix = part;   // inclusive suffix sum over lanes >= this one
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const uint32_t y = __shfl_down_sync(0xffffffffu, suffix, o);
+    if (lane + o < 32) suffix += y;
+  }
+  const uint32_t above = __shfl_down_sync(0xffffffffu, suffix, 1);
+  const uint32_t above_l = lane < 31 ? above : 0u;
+  int found = -1;
+  if (suffix >= (uint32_t)kk && above_l < (uint32_t)kk) {
+    uint32_t run = above_l;
+    for (int b = PER - 1; b >= 0; --b) {
+      run += __ldcg(hist + lane * PER + b);
+      if (run >= (uint32_t)kk) {
+        found = lane * PER + b;
+        break;
+      }
+    }
+  }
+  const uint32_t m = __ballot_sync(0xffffffffu, found >= 0);
+  return m ? __shfl_sync(0xffffffffu, found, __ffs(m) - 1) : 0;
+}
+
+// The same search over a histogram in shared memory, also returning the count strictly above the bin.
+static __device__ int warp_boundary_bin_smem(const uint32_t* hist, int64_t kk, uint32_t* above_out) {
+  const int lane = threadIdx.x & 31;
+  constexpr int PER = NBINS / 32;
+  uint32_t part = 0;
+  for (int i = 0; i < PER; ++i) part += hist[lane * PER + ((i + lane) & (PER - 1))];   // skewed: no bank conflicts
+  uint32_t suffix = part;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const uint32_t y = __shfl_down_sync(0xffffffffu, suffix, o);
+    if (lane + o < 32) suffix += y;
+  }
+  const uint32_t above = __shfl_down_sync(0xffffffffu, suffix, 1);
+  const uint32_t above_l = lane < 31 ? above : 0u;
+  int found = -1;
+  uint32_t found_above = 0;
+  if (suffix >= (uint32_t)kk && above_l < (uint32_t)kk) {
+    uint32_t run = above_l;
+    for (int b = PER - 1; b >= 0; --b) {
+      const uint32_t h = hist[lane * PER + b];
+      if (run + h >= (uint32_t)kk) {
+        found = lane * PER + b;
+        found_above = run;
+        break;
+      }
+      run += h;
+    }
+  }
+  const uint32_t m = __ballot_sync(0xffffffffu, found >= 0);
+  const int src = m ? __ffs(m) - 1 : 0;
+  *above_out = __shfl_sync(0xffffffffu, found_above, src);
+  return m ? __shfl_sync(0xffffffffu, found, src) : 0;
+}
+
+// The whole selection over score rows (workspace memset, histogram, collect, finalize): see select.cu.
+int launch_select(const float* scores, int64_t rows, int64_t n, int64_t row_stride, int64_t kk, int64_t mask_lo,
+                  int64_t mask_hi, int64_t index_offset, int64_t* out_idx, int64_t out_stride, float* out_scores,
+                  int64_t append_sink, int64_t append_local, void* workspace, size_t workspace_bytes,
+                  cudaStream_t st);
 
 }  // namespace selectk
 }  // namespace fathom

@@ -104,10 +104,9 @@ int fathom_scan(const float* q, int64_t BH, int G, int64_t n, int64_t sub, const
 /* Workspace bytes of fathom_scan_select. */
 size_t fathom_scan_select_workspace_bytes(int64_t BH, int G, int64_t n, int64_t kk);
 
-/* The scan fused with the histogram pass of the selection: PlaneStore.scan followed by
- * sink_local_topk (kernels/bitplane.py:319-338, 372-378) in four launches (memset, scan with the
- * histogram in its epilogue, collect, finalize) instead of six; the scores are not re-read for the
- * histogram.  Writes scores [BH][G][n] (all blocks) and, per row r = bh*G+g, the top-kk of tokens in
+/* PlaneStore.scan followed by sink_local_topk-style selection in one call (kernels/bitplane.py:319-338,
+ * 372-378): the scan, then the selection's histogram / collect / finalize passes, all on the stream.
+ * Writes scores [BH][G][n] (all blocks) and, per row r = bh*G+g, the top-kk of tokens in
  * [mask_lo, mask_hi) plus index_offset to out_idx [r][out_stride] in (score desc, index asc) order,
  * followed by 0..append_sink-1 and n-append_local..n-1; the selected scores to out_scores [r][kk] if
  * not NULL.  sink_local_topk(k, sink, local) is kk = k-sink-local, mask [sink, n-local), offset 0,
@@ -154,11 +153,11 @@ int fathom_sink_local_topk(const float* scores, int64_t rows, int64_t n, int64_t
 int fathom_sink_local_topk_static(const float* scores, int64_t rows, int64_t n, int64_t k, int64_t sink,
                                   int64_t local, int64_t* idx, void* stream);
 
-/* Final top-kk of candidate lists [rows][m] (scores, global int64 indices < 2^32) in the
+/* Final top-kk of candidate lists [rows][m] (scores, distinct global int64 indices < 2^32) in the
  * (score descending, index ascending) order: the merge of per-shard candidates of a
  * context-sharded scan.  No reference counterpart (the reference runs on one GPU);
  * it restates the top-k of sink_local_topk (kernels/bitplane.py:376) over a union.
- * m in 1..8192, kk <= m. */
+ * m in 1..8192, kk <= min(m, 4096). */
 int fathom_merge_topk(const float* cand_scores, const int64_t* cand_idx, int64_t rows, int64_t m, int64_t kk,
                       int64_t* out_idx, float* out_scores, void* stream);
 

@@ -131,8 +131,8 @@ def test_sharded_select_emulated_equals_single(world):
 @pytest.mark.parametrize("G,n,k", [(4, 131072, 580), (4, 700, 100), (7, 33000, 2116), (1, 5000, 300), (8, 20000, 1000)])
 @pytest.mark.parametrize("sub", [16, "nblk"])
 def test_scan_topk_fused_equals_unfused(G, n, k, sub):
-    """The scan with the selection histogram in its epilogue selects exactly what scan + sink_local_topk
-    selects (same scores, same order)."""
+    """scan_topk / scan_select in one call select exactly what scan + sink_local_topk selects (same scores,
+    same order)."""
     import math
     from fathom_b200 import bitplane as bp
     from fathom_b200.synth import make_layer
