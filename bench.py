@@ -513,6 +513,12 @@ def main():
                                 "sample": f"{a.cpu_heads} KV heads x {a.ctx} tokens of one layer: plan+scan+"
                                           f"sink_local_topk+attention, numpy oracle ({t:.1f} s)"}
     if rank == 0:
+        # bounded device waits that gave up during the run (NaN-scored tiles); 0 in a valid run
+        import ctypes
+        from fathom_b200 import _lib
+        count = ctypes.c_ulonglong(0)
+        _lib.check(_lib.lib().fathom_wait_timeouts(ctypes.byref(count), 0), "wait_timeouts")
+        line["wait_timeouts"] = int(count.value)
         print(json.dumps(line), flush=True)
     if world > 1:
         torch.distributed.barrier()

@@ -37,6 +37,7 @@ SIGNATURES = {
     "fathom_relayout": (I32, [P, P, I64, I64, I64, P, P, I64, P]),
     "fathom_make_plan": (I32, [P, P, I64, I32, I32, P, P, P, P, P, P, P, P]),
     "fathom_scan": (I32, [P, I64, I32, I64, I64, P, P, I32, P, P, I64, I64, P, P]),
+    "fathom_wait_timeouts": (I32, [P, I32]),
     "fathom_scan_select_workspace_bytes": (SZ, [I64, I32, I64, I64]),
     "fathom_scan_select": (I32, [P, I64, I32, I64, I64, P, P, I32, P, P, I64, I64, I64, I64, I64, I64, P, P, I64, P,
                                  P, SZ, P, P]),

@@ -18,14 +18,26 @@
 // bytes in both the HBM order (sub = 16) and the host run order (sub = nblk).  Every lane keeps
 // G x TPL fp32 accumulators in registers; the query tile and the channel list sit in shared memory.
 //
-// Memory parallelism: the channel list is cut into batches of about WB plane words.  One lane per
-// half-word copies the words (and the 4-byte word holding the block scale) of the next batch into
-// shared memory with cp.async while the warp computes the current batch from the other buffer, so
-// a warp keeps a whole batch in flight instead of one channel.  Lanes sharing a half-word read the
-// copy after cp.async.wait_group and a warp barrier; a second warp barrier guards buffer reuse.
+// Memory parallelism: the channel list is cut into batches of about WB plane words.  The CTA copies
+// the plane words of the next batch into shared memory while it computes the current batch from
+// the other buffer, so a whole batch stays in flight.  Three copy modes, picked by the launch from
+// the superblock order:
+//   BULK  (sub a multiple of the CTA tile, e.g. the host run order): the whole tile of a (channel,
+//         plane) is one contiguous run of tile_blocks * 8 bytes, and of a channel's scales one of
+//         tile_blocks * 2 bytes; one warp issues one cp.async.bulk per run, completing on a
+//         per-buffer mbarrier.  Over the host link these reach ~51 GB/s.
+//   VEC16 (sub even and below the tile, the HBM order): the CTA copies 16-byte chunks (2 blocks)
+//         with cp.async; fastest from HBM, but only ~36 GB/s from host memory.
+//   LANE4 (anything else): one lane per half-word copies 4 bytes with cp.async (~47 GB/s host).
+// Outside BULK, block scales are 4-byte copies of the aligned word holding each lane's scale.
+// Block barriers order the copies against their readers and guard buffer reuse.  Every mbarrier
+// wait is bounded: a wait that gives up counts in a device counter the host reads back
+// (fathom_wait_timeouts), the CTA stops issuing, waits (bounded again) for its copies in flight and
+// writes NaN scores.
 #include "select_common.cuh"
 
 #include <stdlib.h>
+#include <string.h>
 
 namespace fathom {
 namespace {
@@ -35,12 +47,55 @@ constexpr int WB = 32;            // a batch holds the channels whose first word
 constexpr int WBUF = WB + 3;      // ... so its words span at most WB + 3 slots
 constexpr int CB = WB;            // and at most WB channels (each has >= 1 word)
 template <int TPL>
-constexpr int stage_u32() { return (WBUF + CB) * (32 * TPL / 32); }  // one buffer of one warp: (WBUF+CB) x half-words
+constexpr int stage_u32() { return (WBUF + CB) * WARPS * TPL; }   // one CTA buffer: (WBUF+CB) rows x tile half-words
 constexpr int MAXB = D * NPLANES / WB + 2;   // batch boundaries
+enum CopyMode : int { COPY_LANE4 = 0, COPY_VEC16 = 1, COPY_BULK = 2 };
+constexpr unsigned long long WAIT_LIMIT_NS = 2000000000ull;   // 2 s per mbarrier wait
+
+__device__ unsigned long long g_wait_timeouts = 0;   // bounded waits that gave up (host-readable)
 
 __device__ __forceinline__ void cp_async4(uint32_t* smem_dst, const void* gsrc) {
   const uint32_t d = static_cast<uint32_t>(__cvta_generic_to_shared(smem_dst));
   asm volatile("cp.async.ca.shared.global [%0], [%1], 4;\n" ::"r"(d), "l"(gsrc) : "memory");
+}
+__device__ __forceinline__ void cp_async16(uint32_t* smem_dst, const void* gsrc) {
+  const uint32_t d = static_cast<uint32_t>(__cvta_generic_to_shared(smem_dst));
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(d), "l"(gsrc) : "memory");
+}
+__device__ __forceinline__ void mbar_init(uint64_t* mb) {
+  const uint32_t a = static_cast<uint32_t>(__cvta_generic_to_shared(mb));
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;\n" ::"r"(a) : "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* mb, uint32_t bytes) {
+  const uint32_t a = static_cast<uint32_t>(__cvta_generic_to_shared(mb));
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n" ::"r"(a), "r"(bytes) : "memory");
+}
+// global -> this CTA's shared memory, no multicast; 16-byte aligned addresses, size a multiple of 16
+__device__ __forceinline__ void bulk_g2s(uint32_t* smem_dst, const void* gsrc, uint32_t bytes, uint64_t* mb) {
+  const uint32_t d = static_cast<uint32_t>(__cvta_generic_to_shared(smem_dst));
+  const uint32_t a = static_cast<uint32_t>(__cvta_generic_to_shared(mb));
+  asm volatile("cp.async.bulk.shared::cta.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];\n" ::"r"(d),
+               "l"(gsrc), "r"(bytes), "r"(a)
+               : "memory");
+}
+__device__ __forceinline__ unsigned long long global_ns() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+// Waits until the phase with this parity completes; false after WAIT_LIMIT_NS.
+__device__ __forceinline__ bool mbar_wait(uint64_t* mb, uint32_t parity) {
+  const uint32_t a = static_cast<uint32_t>(__cvta_generic_to_shared(mb));
+  uint32_t done = 0;
+  const unsigned long long t0 = global_ns();
+  while (true) {
+    asm volatile("{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2; selp.u32 %0, 1, 0, p; }\n"
+                 : "=r"(done)
+                 : "r"(a), "r"(parity)
+                 : "memory");
+    if (done) return true;
+    if (global_ns() - t0 > WAIT_LIMIT_NS) return false;
+  }
 }
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
 template <int N>
@@ -68,29 +123,37 @@ __device__ __forceinline__ void tokens(float (&acc)[G][TPL], const uint32_t (&w)
 template <int TPL, int G>
 constexpr int min_blocks() { return TPL == 32 ? 2 : TPL == 16 ? (G > 4 ? 2 : 3) : (G > 4 ? 3 : 5); }
 
-template <int G, int TPL>
+template <int G, int TPL, bool BULK>
 __global__ void __launch_bounds__(WARPS * 32, (min_blocks<TPL, G>()))
     scan_kernel(const float* __restrict__ q, const int32_t* __restrict__ cls, const int32_t* __restrict__ clsn,
                 int bmax, const uint32_t* __restrict__ planes32, const uint16_t* __restrict__ scales, int64_t n,
                 int64_t nblk, int64_t nsb, int64_t sub, int64_t blk_begin, int64_t blk_end, int64_t grp_begin,
-                float* __restrict__ out) {
+                int mode, float* __restrict__ out) {
+  // BULK instances run the bulk copies; the others run mode COPY_VEC16 or COPY_LANE4
   constexpr int LPW = 32 / TPL;          // lanes sharing a plane half-word
   constexpr int NHW = 32 / LPW;          // half-words per warp
   constexpr int BPW = NHW / 2;           // blocks per warp
-  constexpr int STAGE_U32 = stage_u32<TPL>();
-  extern __shared__ uint32_t s_stage[];  // [WARPS][2][STAGE_U32]
+  constexpr int TW = WARPS * NHW;        // half-words of the CTA tile (WARPS * BPW blocks)
+  constexpr int CPP = TW / 4;            // 16-byte chunks per (channel, plane) of the tile
+  constexpr int STAGE_U32 = (WBUF + CB) * TW;   // one buffer: WBUF word rows, then CB scale rows
+  constexpr int TILE_BLOCKS = WARPS * BPW;
+  constexpr uint32_t ROW_BYTES = TILE_BLOCKS * 8;     // one (channel, plane) run of the tile
+  constexpr uint32_t SROW_BYTES = TILE_BLOCKS * 2;    // one channel's scales of the tile
+  extern __shared__ __align__(16) uint32_t s_stage[];  // [2][STAGE_U32]
   __shared__ float s_q[G][D];
   __shared__ int s_ch[D], s_t[D], s_slot[D];
-  __shared__ int s_bstart[MAXB + 1];
+  __shared__ uint16_t s_pair[D * NPLANES];     // word position -> channel | plane << 8
+  __shared__ int s_bstart[MAXB + 1], s_wstart[MAXB + 1];
   __shared__ int s_nb;
+  __shared__ __align__(8) uint64_t s_mbar[2];   // BULK: one per stage buffer
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int64_t bh = blockIdx.y;
   for (int e = tid; e < G * D; e += blockDim.x) s_q[e / D][e % D] = q[bh * G * D + e];
   // one round of global loads: the query tile above, and here every thread's column of the four
   // class lists plus the class counts; then the flat channel list in class order (depth 1, 2, 3, 4).
-  // Entry i of class c sits at flat index cstart[c] + i and word slot cword[c] + c * i; its batch
-  // is slot / WB.
+  // Entry i of class c sits at flat index cstart[c] + i and word position cword[c] + c * i; its batch
+  // is position / WB; s_pair maps every word position to its (channel, plane).
   int cnt4[NPLANES];
   int ch4[NPLANES];
 #pragma unroll
@@ -112,7 +175,14 @@ __global__ void __launch_bounds__(WARPS * 32, (min_blocks<TPL, G>()))
     cstart[NPLANES] = st;
   }
   const int total = cstart[NPLANES];
-  if (tid == 0) s_nb = 0;
+  if (tid == 0) {
+    s_nb = 0;
+    if constexpr (BULK) {
+      mbar_init(&s_mbar[0]);
+      mbar_init(&s_mbar[1]);
+      asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");   // visible to the bulk copies
+    }
+  }
   __syncthreads();   // s_nb reset before any thread closes the last batch below
 #pragma unroll
   for (int c = 0; c < NPLANES; ++c) {
@@ -121,8 +191,10 @@ __global__ void __launch_bounds__(WARPS * 32, (min_blocks<TPL, G>()))
       const int m = cstart[c] + i;
       const int t = c + 1;
       const int slot = cword[c] + t * i;
-      s_ch[m] = ch4[c] & (D - 1);                      // channel ids are 0..127
+      const int ch = ch4[c] & (D - 1);                 // channel ids are 0..127
+      s_ch[m] = ch;
       s_t[m] = t;
+      for (int p = 0; p < t; ++p) s_pair[slot + p] = (uint16_t)(ch | (p << 8));
       const int b = slot / WB;
       s_slot[m] = slot - b * WB;
       // the previous flat entry's batch (entry i-1 of this class, or the last of an earlier class)
@@ -135,10 +207,14 @@ __global__ void __launch_bounds__(WARPS * 32, (min_blocks<TPL, G>()))
         }
         prev = (cword[pc] + (pc + 1) * pi) / WB;
       }
-      if (b != prev) s_bstart[b] = m;
+      if (b != prev) {
+        s_bstart[b] = m;
+        s_wstart[b] = slot;
+      }
       if (m == total - 1) {  // the last channel closes the last batch
         s_nb = b + 1;
         s_bstart[b + 1] = m + 1;
+        s_wstart[b + 1] = slot + t;
       }
     }
   }
@@ -146,6 +222,7 @@ __global__ void __launch_bounds__(WARPS * 32, (min_blocks<TPL, G>()))
 
   const int64_t grp = grp_begin + (int64_t)blockIdx.x * WARPS + warp;
   const int64_t wblk0 = grp * BPW;
+  const int64_t tile_blk0 = (grp_begin + (int64_t)blockIdx.x * WARPS) * BPW;
   const int64_t lo = blk_begin > wblk0 ? blk_begin : wblk0;
   const int64_t hi_lim = blk_end < nblk ? blk_end : nblk;
   const bool warp_live = !(lo >= hi_lim || wblk0 + BPW <= blk_begin);  // some block of the warp in range
@@ -162,20 +239,64 @@ __global__ void __launch_bounds__(WARPS * 32, (min_blocks<TPL, G>()))
   const int64_t plane_stride32 = sub * 2;
   const int64_t chan_stride32 = NPLANES * sub * 2;
   const int64_t sc_elem0 = (bh * nsb + sb) * D * sub + s_in;   // scale element of channel 0
-
-  uint32_t* stage = s_stage + warp * 2 * STAGE_U32;
-  const int nbatch = warp_live ? s_nb : 0;
+  const int col = warp * NHW + hw;           // this lane's column in the CTA stage rows
+  const int64_t store_blocks = nsb * sub;    // blocks the store holds (pads included)
+  const int nbatch = s_nb;                   // uniform over the CTA (barriers below)
+  // this thread's 16-byte chunk of the tile: blocks tile_blk0 + 2 * chunk and the next one, which
+  // share a superblock because sub is even whenever the 16-byte path is taken
+  constexpr int PSTEP = WARPS * 32 / CPP;
+  const int chunk = tid % CPP, chunk_row = tid / CPP;
+  const int64_t cblk = tile_blk0 + 2 * chunk;
+  const bool chunk_ok = cblk < store_blocks;
+  const int64_t csb = chunk_ok ? cblk / sub : 0;
+  const uint32_t* chunk_src = planes32 + ((bh * nsb + csb) * D * NPLANES * sub + (cblk - csb * sub)) * 2;
+  const int64_t pstride32 = sub * 2;         // 32-bit words between consecutive (channel, plane) rows
+  // BULK: the tile lies inside one superblock (sub is a multiple of TILE_BLOCKS and tiles start on
+  // multiples of it), so its runs start at these two addresses plus a channel / plane offset
+  const int64_t tsb = tile_blk0 / sub;
+  const uint32_t* tile_planes = planes32 + ((bh * nsb + tsb) * D * NPLANES * sub + (tile_blk0 - tsb * sub)) * 2;
+  const uint16_t* tile_scales = scales + (bh * nsb + tsb) * D * sub + (tile_blk0 - tsb * sub);
+  const int tblk = warp * BPW + (hw >> 1);   // this lane's block within the tile
 
   auto issue = [&](int b) {
-    uint32_t* wbuf = stage + (b & 1) * STAGE_U32;
-    uint32_t* sbuf = wbuf + WBUF * NHW;
-    if (active && issuer) {
+    uint32_t* wbuf = s_stage + (b & 1) * STAGE_U32;
+    uint32_t* sbuf = wbuf + WBUF * TW;
+    if constexpr (BULK) {
+      if (warp == 0) {
+        const int w0 = s_wstart[b], w1 = s_wstart[b + 1], c0 = s_bstart[b], c1 = s_bstart[b + 1];
+        uint64_t* mb = &s_mbar[b & 1];
+        if (lane == 0) mbar_expect_tx(mb, (uint32_t)(w1 - w0) * ROW_BYTES + (uint32_t)(c1 - c0) * SROW_BYTES);
+        __syncwarp();
+        for (int pos = w0 + lane; pos < w1; pos += 32) {
+          const int pc = s_pair[pos];
+          bulk_g2s(wbuf + (pos - b * WB) * TW, tile_planes + ((pc & 0xFF) * NPLANES + (pc >> 8)) * pstride32, ROW_BYTES,
+                   mb);
+        }
+        for (int i = c0 + lane; i < c1; i += 32) bulk_g2s(sbuf + (i - c0) * TW, tile_scales + s_ch[i] * sub, SROW_BYTES, mb);
+      }
+      return;
+    }
+    if (mode == COPY_VEC16) {
+      // plane words: the CTA copies each (channel, plane) of its tile in 16-byte chunks (2 blocks);
+      // thread tid always copies chunk tid % CPP, of every PSTEP-th word position of the batch
+      if (chunk_ok) {
+        const int w1 = s_wstart[b + 1];
+        for (int pos = s_wstart[b] + chunk_row; pos < w1; pos += PSTEP) {
+          const int pc = s_pair[pos];
+          cp_async16(&wbuf[(pos - b * WB) * TW + 4 * chunk], chunk_src + ((pc & 0xFF) * NPLANES + (pc >> 8)) * pstride32);
+        }
+      }
+    } else if (active && issuer) {
       for (int i = s_bstart[b]; i < s_bstart[b + 1]; ++i) {
         const int ch = s_ch[i], t = s_t[i], slot = s_slot[i];
         const uint32_t* gp = pbase + ch * chan_stride32;
-        for (int p = 0; p < t; ++p) cp_async4(&wbuf[(slot + p) * NHW + hw], gp + p * plane_stride32);
-        const int64_t e = sc_elem0 + (int64_t)ch * sub;            // the aligned 4-byte word holding it
-        cp_async4(&sbuf[(i - s_bstart[b]) * NHW + hw], scales + (e & ~(int64_t)1));
+        for (int p = 0; p < t; ++p) cp_async4(&wbuf[(slot + p) * TW + col], gp + p * plane_stride32);
+      }
+    }
+    if (active && issuer) {  // block scales: the aligned 4-byte word holding this lane's scale
+      for (int i = s_bstart[b]; i < s_bstart[b + 1]; ++i) {
+        const int64_t e = sc_elem0 + (int64_t)s_ch[i] * sub;
+        cp_async4(&sbuf[(i - s_bstart[b]) * TW + col], scales + (e & ~(int64_t)1));
       }
     }
     cp_async_commit();
@@ -190,26 +311,46 @@ __global__ void __launch_bounds__(WARPS * 32, (min_blocks<TPL, G>()))
     for (int k = 0; k < TPL; ++k) acc[g][k] = 0.0f;
   }
 
-  if (nbatch > 0) issue(0);
+  bool stalled = false;                    // this thread gave up on an mbarrier wait
+  int issued = 0;                          // batches issued so far (uniform)
+  if (nbatch > 0) {
+    issue(0);
+    issued = 1;
+  }
   for (int b = 0; b < nbatch; ++b) {
-    if (LPW > 1) __syncwarp();             // every lane is done with the buffer issue(b + 1) refills
+    // every thread is done with the buffer issue(b + 1) refills; a stall anywhere stops the CTA
+    if (__syncthreads_or(stalled)) break;
     if (b + 1 < nbatch) {
       issue(b + 1);
-      cp_async_wait<1>();
-    } else {
-      cp_async_wait<0>();
+      issued = b + 2;
     }
-    if (LPW > 1) __syncwarp();             // the issuers' copies are visible to the whole warp
-    const uint32_t* wbuf = stage + (b & 1) * STAGE_U32;
-    const uint32_t* sbuf = wbuf + WBUF * NHW;
+    if constexpr (BULK) {
+      if (!mbar_wait(&s_mbar[b & 1], (b >> 1) & 1)) {
+        stalled = true;
+        atomicAdd(&g_wait_timeouts, 1ull);
+        continue;
+      }
+    } else {
+      if (b + 1 < nbatch) cp_async_wait<1>();
+      else cp_async_wait<0>();
+      __syncthreads();                     // every thread's copies of batch b are visible to the CTA
+    }
+    const uint32_t* wbuf = s_stage + (b & 1) * STAGE_U32;
+    const uint32_t* sbuf = wbuf + WBUF * TW;
     for (int i = s_bstart[b]; i < s_bstart[b + 1]; ++i) {
       const int ch = s_ch[i], t = s_t[i], slot = s_slot[i];
-      const int64_t e = sc_elem0 + (int64_t)ch * sub;
-      const uint32_t sw = sbuf[(i - s_bstart[b]) * NHW + hw];
-      const float sc = active ? __half2float(__ushort_as_half((uint16_t)(sw >> ((e & 1) * 16)))) : 0.0f;
+      float sc;
+      if constexpr (BULK) {
+        sc = __half2float(__ushort_as_half(reinterpret_cast<const uint16_t*>(sbuf + (i - s_bstart[b]) * TW)[tblk]));
+      } else {
+        const int64_t e = sc_elem0 + (int64_t)ch * sub;
+        const uint32_t sw = sbuf[(i - s_bstart[b]) * TW + col];
+        sc = __half2float(__ushort_as_half((uint16_t)(sw >> ((e & 1) * 16))));
+      }
+      sc = active ? sc : 0.0f;
       uint32_t w[4];
 #pragma unroll
-      for (int p = 0; p < 4; ++p) w[p] = (p < t && active) ? (wbuf[(slot + p) * NHW + hw] >> bitoff) : 0u;
+      for (int p = 0; p < 4; ++p) w[p] = (p < t && active) ? (wbuf[(slot + p) * TW + col] >> bitoff) : 0u;
       float W[G];
       const float KC = __uint_as_float(0x3F800000u - ((uint32_t)t << 23)) - 3.0f;   // 2^-t - 3
 #pragma unroll
@@ -226,13 +367,23 @@ __global__ void __launch_bounds__(WARPS * 32, (min_blocks<TPL, G>()))
       }
     }
   }
-  // Epilogue, one query head at a time: the warp's scores go through its (now idle) staging area, so
+  // the stage is reused for the epilogue below; after a stall, first wait (bounded) for the copies
+  // still in flight: the last batch issued into each buffer
+  if (__syncthreads_or(stalled)) {
+    if constexpr (BULK)
+      for (int b = issued - 2 < 0 ? 0 : issued - 2; b < issued; ++b) mbar_wait(&s_mbar[b & 1], (b >> 1) & 1);
+    __syncthreads();
+#pragma unroll
+    for (int g = 0; g < G; ++g) cst[g] = __int_as_float(0x7fc00000);   // NaN scores flag the failed tiles
+  }
+
+  // Epilogue, one query head at a time: the warp's scores go through its slice of the stage, so
   // the global stores are fully coalesced (512 contiguous bytes per warp instruction).
   // Lane l owns warp tokens l*TPL .. l*TPL+TPL-1; float4 slot j of lane l's row is stored at
   // j ^ swz(l), which keeps both the row writes and the token-order reads free of bank conflicts.
   constexpr int R = TPL / 4;                       // float4 per lane row
   constexpr int ROWS_PER_128B = 8 / R;
-  float* s_sc = reinterpret_cast<float*>(stage);   // 32 * TPL floats
+  float* s_sc = reinterpret_cast<float*>(s_stage) + warp * 32 * TPL;   // 32 * TPL floats per warp
   const int64_t wtok0 = wblk0 * BLK;               // first token of the warp
   const int64_t tok_lo = (warp_live ? lo : 0) * BLK;
   const int64_t tok_hi = warp_live ? (hi_lim * BLK < n ? hi_lim * BLK : n) : 0;   // valid tokens: [tok_lo, tok_hi)
@@ -274,14 +425,26 @@ int launch_scan(const float* q, int64_t BH, int64_t n, int64_t nblk, int64_t nsb
                 const int32_t* clsn, int bmax, const uint32_t* planes32, const uint16_t* scales, int64_t b0, int64_t b1,
                 float* out, cudaStream_t st) {
   constexpr int BPW = TPL / 2;
-  const int64_t g0 = b0 / BPW, g1 = cdiv(b1, BPW);
+  constexpr int TILE_BLOCKS = WARPS * BPW;
+  const int64_t g0 = b0 / TILE_BLOCKS * WARPS, g1 = cdiv(b1, BPW);   // tiles start on multiples of TILE_BLOCKS
   const int64_t grid_x = cdiv(g1 - g0, WARPS);
   FATHOM_REQUIRE(grid_x <= 0x7fffffffLL && BH <= 65535, FATHOM_ERR_SHAPE, "scan: grid too large");
-  const size_t smem = (size_t)WARPS * 2 * stage_u32<TPL>() * sizeof(uint32_t);
-  cudaFuncSetAttribute(scan_kernel<G, TPL>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  const size_t smem = (size_t)2 * stage_u32<TPL>() * sizeof(uint32_t);
+  // BULK needs each tile inside one superblock and 16-byte aligned runs; VEC16 needs every 2-block
+  // pair contiguous and 16-byte aligned
+  const bool a16 = (reinterpret_cast<uintptr_t>(planes32) & 15) == 0;
+  const bool bulk_ok = a16 && (reinterpret_cast<uintptr_t>(scales) & 15) == 0 && sub % TILE_BLOCKS == 0;
+  const bool vec16_ok = a16 && sub % 2 == 0;
+  int mode = bulk_ok ? COPY_BULK : (vec16_ok && sub < TILE_BLOCKS) ? COPY_VEC16 : COPY_LANE4;
+  if (const char* env = getenv("FATHOM_SCAN_COPY")) {   // tuning override: bulk, 16 or 4 (when the layout allows)
+    if (!strcmp(env, "4")) mode = COPY_LANE4;
+    else if (!strcmp(env, "16") && vec16_ok) mode = COPY_VEC16;
+    else if (!strcmp(env, "bulk") && bulk_ok) mode = COPY_BULK;
+  }
+  auto kernel = mode == COPY_BULK ? scan_kernel<G, TPL, true> : scan_kernel<G, TPL, false>;
+  cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   dim3 grid((unsigned)grid_x, (unsigned)BH);
-  scan_kernel<G, TPL><<<grid, WARPS * 32, smem, st>>>(q, cls, clsn, bmax, planes32, scales, n, nblk, nsb, sub, b0, b1,
-                                                      g0, out);
+  kernel<<<grid, WARPS * 32, smem, st>>>(q, cls, clsn, bmax, planes32, scales, n, nblk, nsb, sub, b0, b1, g0, mode, out);
   return check_launch("scan");
 }
 
@@ -397,4 +560,16 @@ extern "C" int fathom_scan_select(const float* q, int64_t BH, int G, int64_t n, 
   }
   return selectk::launch_select(scores, rows, n, n, kk, mask_lo, mask_hi, index_offset, out_idx, out_stride,
                                 out_scores, append_sink, append_local, workspace, workspace_bytes, st);
+}
+
+extern "C" int fathom_wait_timeouts(unsigned long long* count, int reset) {
+  unsigned long long v = 0;
+  cudaError_t e = cudaMemcpyFromSymbol(&v, g_wait_timeouts, sizeof(v));
+  if (e == cudaSuccess && reset) {
+    const unsigned long long zero = 0;
+    e = cudaMemcpyToSymbol(g_wait_timeouts, &zero, sizeof(zero));
+  }
+  if (e != cudaSuccess) return set_error(FATHOM_ERR_CUDA, "wait_timeouts: %s", cudaGetErrorString(e));
+  if (count) *count = v;
+  return FATHOM_OK;
 }

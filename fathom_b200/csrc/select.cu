@@ -60,10 +60,28 @@ __global__ void __launch_bounds__(HT) hist_kernel(const float* __restrict__ scor
   const int64_t i0 = (int64_t)blockIdx.x * CHUNK;
   const int64_t i1 = i0 + CHUNK < n ? i0 + CHUNK : n;
   const bool vec = (n % 4 == 0) && (row_stride % 4 == 0) && ((reinterpret_cast<uintptr_t>(scores) & 15) == 0);
-  for_each_score(r, i0, i1, vec, [&](int64_t i, float x) {
-    const uint32_t key = (i >= mask_lo && i < mask_hi) ? f2key(x) : KEY_NEG_INF;
-    atomicAdd(&sh[key >> (32 - HBITS)], 1u);
-  });
+  const bool unmasked = i0 >= mask_lo && i1 <= mask_hi;
+  constexpr int PER = CHUNK / HT;                  // 32 scores per thread, loaded before any atomic
+  float x[PER];
+#pragma unroll
+  for (int u = 0; u < PER / 4; ++u) {
+    const int64_t i = i0 + 4 * ((int64_t)threadIdx.x + (int64_t)u * HT);
+    if (vec) {
+      const float4 v = i < i1 ? *reinterpret_cast<const float4*>(r + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+      x[4 * u] = v.x; x[4 * u + 1] = v.y; x[4 * u + 2] = v.z; x[4 * u + 3] = v.w;
+    } else {
+#pragma unroll
+      for (int e = 0; e < 4; ++e) x[4 * u + e] = i + e < i1 ? r[i + e] : 0.f;
+    }
+  }
+#pragma unroll
+  for (int u = 0; u < PER; ++u) {
+    const int64_t i = i0 + 4 * ((int64_t)threadIdx.x + (int64_t)(u / 4) * HT) + (u % 4);
+    if (i < i1) {
+      const uint32_t key = (unmasked || (i >= mask_lo && i < mask_hi)) ? f2key(x[u]) : KEY_NEG_INF;
+      atomicAdd(&sh[key >> (32 - HBITS)], 1u);
+    }
+  }
   __syncthreads();
   uint32_t* gh = ghist + row * NBINS;
   for (int b = threadIdx.x; b < NBINS; b += HT)
@@ -79,11 +97,12 @@ __global__ void __launch_bounds__(HT) hist_kernel(const float* __restrict__ scor
   if (threadIdx.x == 0) bstar[row] = (uint32_t)bs;
 }
 
-__global__ void __launch_bounds__(HT) collect_kernel(const float* __restrict__ scores, int64_t n, int64_t row_stride,
+__global__ void __launch_bounds__(HT, 2) collect_kernel(const float* __restrict__ scores, int64_t n, int64_t row_stride,
                                                      int64_t mask_lo, int64_t mask_hi,
                                                      const uint32_t* __restrict__ bstar_rows,
                                                      uint32_t* __restrict__ count, uint64_t* __restrict__ cand) {
-  constexpr int PER = CHUNK / HT;           // scores per thread (32)
+  constexpr int PER = CHUNK / HT;           // scores per thread (32), in two rounds of 16
+  constexpr int HALF = PER / 2;
   const int64_t row = blockIdx.y;
   const uint32_t bstar = bstar_rows[row];
   const float* r = scores + row * row_stride;
@@ -92,45 +111,47 @@ __global__ void __launch_bounds__(HT) collect_kernel(const float* __restrict__ s
   const int lane = threadIdx.x & 31;
   uint64_t* cr = cand + row * CAP;
   const bool vec = (n % 4 == 0) && (row_stride % 4 == 0) && ((reinterpret_cast<uintptr_t>(scores) & 15) == 0);
-  // all loads of this thread first (thread t owns scores i0 + 4t + 4*HT*u + e), then the filter
-  float x[PER];
-  if (vec) {
-#pragma unroll
-    for (int u = 0; u < PER / 4; ++u) {
-      const int64_t i = i0 + 4 * ((int64_t)threadIdx.x + (int64_t)u * HT);
-      const float4 v = i < i1 ? *reinterpret_cast<const float4*>(r + i) : make_float4(0.f, 0.f, 0.f, 0.f);
-      x[4 * u] = v.x; x[4 * u + 1] = v.y; x[4 * u + 2] = v.z; x[4 * u + 3] = v.w;
-    }
-  } else {
-#pragma unroll
-    for (int u = 0; u < PER; ++u) {
-      const int64_t i = i0 + 4 * ((int64_t)threadIdx.x + (int64_t)(u / 4) * HT) + (u % 4);
-      x[u] = i < i1 ? r[i] : 0.f;
-    }
-  }
-  // which of this thread's scores are candidates (a bit per score); most warps have none
   const bool unmasked = i0 >= mask_lo && i1 <= mask_hi;   // the whole chunk is outside sink/local
-  uint32_t takes = 0;
+#pragma unroll 1
+  for (int round = 0; round < 2; ++round) {
+    // thread t owns scores i0 + 4t + 4*HT*u + e; this round's loads first, then the filter
+    float x[HALF];
 #pragma unroll
-  for (int u = 0; u < PER; ++u) {
-    const int64_t i = i0 + 4 * ((int64_t)threadIdx.x + (int64_t)(u / 4) * HT) + (u % 4);
-    const uint32_t key = (unmasked || (i >= mask_lo && i < mask_hi)) ? f2key(x[u]) : KEY_NEG_INF;
-    if (i < i1 && (key >> (32 - HBITS)) >= bstar) takes |= 1u << u;
-  }
-  if (!__any_sync(0xffffffffu, takes != 0)) return;
+    for (int uu = 0; uu < HALF / 4; ++uu) {
+      const int u = round * (HALF / 4) + uu;
+      const int64_t i = i0 + 4 * ((int64_t)threadIdx.x + (int64_t)u * HT);
+      if (vec) {
+        const float4 v = i < i1 ? *reinterpret_cast<const float4*>(r + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+        x[4 * uu] = v.x; x[4 * uu + 1] = v.y; x[4 * uu + 2] = v.z; x[4 * uu + 3] = v.w;
+      } else {
 #pragma unroll
-  for (int u = 0; u < PER; ++u) {
-    const int64_t i = i0 + 4 * ((int64_t)threadIdx.x + (int64_t)(u / 4) * HT) + (u % 4);
-    const bool take = (takes >> u) & 1u;
-    const uint32_t m = __ballot_sync(0xffffffffu, take);
-    if (m) {
-      uint32_t pos0 = 0;
-      if (lane == 0) pos0 = atomicAdd(&count[row], (uint32_t)__popc(m));
-      pos0 = __shfl_sync(0xffffffffu, pos0, 0);
-      if (take) {
-        const uint32_t key = (unmasked || (i >= mask_lo && i < mask_hi)) ? f2key(x[u]) : KEY_NEG_INF;
-        const uint32_t pos = pos0 + __popc(m & ((1u << lane) - 1));
-        if (pos < CAP) cr[pos] = ((uint64_t)key << 32) | (uint32_t)(~(uint32_t)i);
+        for (int e = 0; e < 4; ++e) x[4 * uu + e] = i + e < i1 ? r[i + e] : 0.f;
+      }
+    }
+    uint32_t takes = 0;
+#pragma unroll
+    for (int v = 0; v < HALF; ++v) {
+      const int u = round * (HALF / 4) + v / 4;
+      const int64_t i = i0 + 4 * ((int64_t)threadIdx.x + (int64_t)u * HT) + (v % 4);
+      const uint32_t key = (unmasked || (i >= mask_lo && i < mask_hi)) ? f2key(x[v]) : KEY_NEG_INF;
+      if (i < i1 && (key >> (32 - HBITS)) >= bstar) takes |= 1u << v;
+    }
+    if (!__any_sync(0xffffffffu, takes != 0)) continue;
+#pragma unroll
+    for (int v = 0; v < HALF; ++v) {
+      const int u = round * (HALF / 4) + v / 4;
+      const int64_t i = i0 + 4 * ((int64_t)threadIdx.x + (int64_t)u * HT) + (v % 4);
+      const bool take = (takes >> v) & 1u;
+      const uint32_t m = __ballot_sync(0xffffffffu, take);
+      if (m) {
+        uint32_t pos0 = 0;
+        if (lane == 0) pos0 = atomicAdd(&count[row], (uint32_t)__popc(m));
+        pos0 = __shfl_sync(0xffffffffu, pos0, 0);
+        if (take) {
+          const uint32_t key = (unmasked || (i >= mask_lo && i < mask_hi)) ? f2key(x[v]) : KEY_NEG_INF;
+          const uint32_t pos = pos0 + __popc(m & ((1u << lane) - 1));
+          if (pos < CAP) cr[pos] = ((uint64_t)key << 32) | (uint32_t)(~(uint32_t)i);
+        }
       }
     }
   }

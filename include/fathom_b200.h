@@ -101,6 +101,12 @@ int fathom_scan(const float* q, int64_t BH, int G, int64_t n, int64_t sub, const
                 int bmax, const uint64_t* planes_k, const uint16_t* scales_k, int64_t blk_begin, int64_t blk_end,
                 float* scores, void* stream);
 
+/* Diagnostic, no reference counterpart: the number of bounded device waits that gave up on the
+ * current device since the last reset (the scan's bulk-copy mbarrier waits, 2 s each).  A wait
+ * that gives up makes its tile's scores NaN; 0 in normal operation.  Synchronises the device.
+ *   count may be NULL; reset != 0 zeroes the counter after reading it. */
+int fathom_wait_timeouts(unsigned long long* count, int reset);
+
 /* Workspace bytes of fathom_scan_select. */
 size_t fathom_scan_select_workspace_bytes(int64_t BH, int G, int64_t n, int64_t kk);
 

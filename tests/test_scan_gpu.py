@@ -1,5 +1,6 @@
 """Plane-prefix scan on the GPU against the reference's scores (golden fixtures) and the oracle,
 in the HBM order, the host run order, and from pinned mapped host memory (zero-copy)."""
+import ctypes
 import math
 
 import numpy as np
@@ -83,13 +84,15 @@ def test_scan_block_range_and_out():
     assert torch.all(out2[..., :3 * 64] == 7.0) and torch.all(out2[..., 9 * 64:] == 7.0)
 
 
-def test_host_store_zero_copy_equals_hbm():
+@pytest.mark.parametrize("n", [20000, 20480])
+def test_host_store_zero_copy_equals_hbm(n):
     """Host run order in pinned mapped memory, read over the host link by the same kernel: bit-identical
-    to the HBM store's scores."""
+    to the HBM store's scores (313 blocks: per-lane copies; 320 blocks: bulk copies of whole tiles)."""
+    from fathom_b200 import _lib
     from fathom_b200 import bitplane as bp
     from fathom_b200.offload import HostPlaneStore
     from fathom_b200.synth import make_layer
-    d = make_layer(4, 4, 20000, seed=3, kv_dtype=torch.bfloat16, with_v=False)
+    d = make_layer(4, 4, n, seed=3, kv_dtype=torch.bfloat16, with_v=False)
     K = d["K"].cuda()
     hs = HostPlaneStore(K)
     hb = bp.PlaneStore(K)
@@ -97,7 +100,10 @@ def test_host_store_zero_copy_equals_hbm():
     q = d["q"].cuda()
     a, b = hs.scan(q, plan), hb.scan(q, plan)
     assert torch.equal(a, b)
-    assert hs.sub == math.ceil(20000 / 64) and hs.nsb == 1
+    count = ctypes.c_ulonglong(1)
+    _lib.check(_lib.lib().fathom_wait_timeouts(ctypes.byref(count), 0), "wait_timeouts")
+    assert count.value == 0
+    assert hs.sub == math.ceil(n / 64) and hs.nsb == 1
     code, sc = O.quantise_u4(d["K"].float().numpy())
     pk, sk = O.to_superblocks(O.pack_planes(code), sc, hs.sub)
     assert np.array_equal(hs.planes_buf.host.numpy().view(np.uint64), pk)
@@ -151,3 +157,34 @@ def test_scan_token_splits(tpl, G, n, monkeypatch):
     out = torch.full_like(s, 5.0)
     st.scan(q, plan, out=out, blocks=(1, 3))
     assert torch.equal(out[..., 64:192], s[..., 64:192]) and torch.all(out[..., :64] == 5.0)
+
+
+@pytest.mark.parametrize("tpl", ["8", "16", "32"])
+@pytest.mark.parametrize("sub", [1, 2, 3, 6, 16, 64, "nblk"])
+def test_scan_layouts_and_copy_paths(sub, tpl, monkeypatch):
+    """Every superblock order gives bit-identical scores: even orders take the CTA's 16-byte copies,
+    odd orders and a planes array that is only 8-byte aligned take the per-lane 4-byte copies."""
+    from fathom_b200 import bitplane as bp
+    from fathom_b200.synth import make_layer
+    monkeypatch.setenv("FATHOM_SCAN_TPL", tpl)
+    n = 64 * 37 + 21                      # 38 blocks: ragged last block, odd tile tail
+    d = make_layer(2, 4, n, seed=11, layer=2, with_v=False)
+    K = d["K"].cuda()
+    ref = bp.PlaneStore(K)
+    plan = bp.make_plan(d["g"].cuda(), 64.0)
+    q = d["q"].cuda()
+    want = ref.scan(q, plan)
+    old = bp.SUB
+    try:
+        bp.SUB = math.ceil(n / 64) if sub == "nblk" else sub
+        st = bp.PlaneStore(K)
+    finally:
+        bp.SUB = old
+    assert torch.equal(st.scan(q, plan), want)
+    # the same words at an address that is 8 but not 16 bytes aligned
+    buf = torch.zeros(st.planes_k.numel() + 1, dtype=torch.int64, device="cuda")
+    buf[1:] = st.planes_k.reshape(-1)
+    st.planes_k = buf[1:].view(st.planes_k.shape)
+    st.planes32 = st.planes_k.view(torch.int32)
+    assert st.planes32.data_ptr() % 16 == 8
+    assert torch.equal(st.scan(q, plan), want)
