@@ -128,7 +128,7 @@ __global__ void __launch_bounds__(WARPS * 32, (min_blocks<TPL, G>()))
     scan_kernel(const float* __restrict__ q, const int32_t* __restrict__ cls, const int32_t* __restrict__ clsn,
                 int bmax, const uint32_t* __restrict__ planes32, const uint16_t* __restrict__ scales, int64_t n,
                 int64_t nblk, int64_t nsb, int64_t sub, int64_t blk_begin, int64_t blk_end, int64_t grp_begin,
-                int mode, float* __restrict__ out) {
+                int mode, float* __restrict__ out, uint32_t* __restrict__ gkey, int64_t ng) {
   // BULK instances run the bulk copies; the others run mode COPY_VEC16 or COPY_LANE4
   constexpr int LPW = 32 / TPL;          // lanes sharing a plane half-word
   constexpr int NHW = 32 / LPW;          // half-words per warp
@@ -389,14 +389,34 @@ __global__ void __launch_bounds__(WARPS * 32, (min_blocks<TPL, G>()))
   const int64_t tok_hi = warp_live ? (hi_lim * BLK < n ? hi_lim * BLK : n) : 0;   // valid tokens: [tok_lo, tok_hi)
   auto swz = [](int row) { return (row / ROWS_PER_128B) & (R - 1); };
   const bool vec_ok = (n % 4 == 0) && ((reinterpret_cast<uintptr_t>(out) & 15) == 0);
+  // group keys for the selection (gkey != NULL): the largest key of each GROUP-token group, from the
+  // same floats the stores below write; a group spans GL lanes
+  constexpr int GL = selectk::GROUP / TPL;
+  const int64_t ltok0 = wtok0 + (int64_t)lane * TPL;   // this lane's first token
 #pragma unroll
   for (int g = 0; g < G; ++g) {
     __syncwarp();
+    uint32_t gm = 0;
 #pragma unroll
-    for (int j = 0; j < R; ++j)
-      reinterpret_cast<float4*>(s_sc)[lane * R + (j ^ swz(lane))] =
-          make_float4(acc[g][4 * j] + cst[g], acc[g][4 * j + 1] + cst[g], acc[g][4 * j + 2] + cst[g],
-                      acc[g][4 * j + 3] + cst[g]);
+    for (int j = 0; j < R; ++j) {
+      const float4 v = make_float4(acc[g][4 * j] + cst[g], acc[g][4 * j + 1] + cst[g], acc[g][4 * j + 2] + cst[g],
+                                   acc[g][4 * j + 3] + cst[g]);
+      reinterpret_cast<float4*>(s_sc)[lane * R + (j ^ swz(lane))] = v;
+      if (gkey) {
+        const float e[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const int64_t t = ltok0 + 4 * j + u;
+          if (t >= tok_lo && t < tok_hi) gm = max(gm, f2key(e[u]));
+        }
+      }
+    }
+    if (gkey) {
+#pragma unroll
+      for (int o = 1; o < GL; o <<= 1) gm = max(gm, __shfl_xor_sync(0xffffffffu, gm, o));
+      const int64_t grp = ltok0 / selectk::GROUP;
+      if (lane % GL == 0 && ltok0 >= tok_lo && ltok0 < tok_hi) gkey[(bh * G + g) * ng + grp] = gm;
+    }
     __syncwarp();
     if (warp_live) {
       float* o = out + (bh * G + g) * n;
@@ -423,7 +443,7 @@ __global__ void __launch_bounds__(WARPS * 32, (min_blocks<TPL, G>()))
 template <int G, int TPL>
 int launch_scan(const float* q, int64_t BH, int64_t n, int64_t nblk, int64_t nsb, int64_t sub, const int32_t* cls,
                 const int32_t* clsn, int bmax, const uint32_t* planes32, const uint16_t* scales, int64_t b0, int64_t b1,
-                float* out, cudaStream_t st) {
+                float* out, uint32_t* gkey, cudaStream_t st) {
   constexpr int BPW = TPL / 2;
   constexpr int TILE_BLOCKS = WARPS * BPW;
   const int64_t g0 = b0 / TILE_BLOCKS * WARPS, g1 = cdiv(b1, BPW);   // tiles start on multiples of TILE_BLOCKS
@@ -444,7 +464,8 @@ int launch_scan(const float* q, int64_t BH, int64_t n, int64_t nblk, int64_t nsb
   auto kernel = mode == COPY_BULK ? scan_kernel<G, TPL, true> : scan_kernel<G, TPL, false>;
   cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   dim3 grid((unsigned)grid_x, (unsigned)BH);
-  kernel<<<grid, WARPS * 32, smem, st>>>(q, cls, clsn, bmax, planes32, scales, n, nblk, nsb, sub, b0, b1, g0, mode, out);
+  kernel<<<grid, WARPS * 32, smem, st>>>(q, cls, clsn, bmax, planes32, scales, n, nblk, nsb, sub, b0, b1, g0, mode, out,
+                                         gkey, selectk::n_groups(n));
   return check_launch("scan");
 }
 
@@ -469,7 +490,7 @@ int sm_count() {
 
 int scan_dispatch(const float* q, int64_t BH, int G, int64_t n, int64_t sub, const int32_t* cls, const int32_t* clsn,
                   int bmax, const uint64_t* planes_k, const uint16_t* scales_k, int64_t blk_begin, int64_t blk_end,
-                  float* scores, cudaStream_t st) {
+                  float* scores, uint32_t* gkey, cudaStream_t st) {
   FATHOM_REQUIRE(q && cls && clsn && planes_k && scales_k && scores, FATHOM_ERR_NULL, "scan: NULL pointer");
   FATHOM_REQUIRE(BH >= 1 && BH <= 65535 && n >= 1 && sub >= 1, FATHOM_ERR_SHAPE, "scan: bad shape (BH=%lld n=%lld)",
                  (long long)BH, (long long)n);
@@ -494,7 +515,8 @@ int scan_dispatch(const float* q, int64_t BH, int G, int64_t n, int64_t sub, con
     if (v == 8 || v == 16 || (v == 32 && G <= 4)) tpl = v;
   }
 #define FATHOM_SCAN_LAUNCH(GG, TT) \
-  return launch_scan<GG, TT>(q, BH, n, nblk, nsb, sub, cls, clsn, bmax, p32, scales_k, blk_begin, blk_end, scores, st);
+  return launch_scan<GG, TT>(q, BH, n, nblk, nsb, sub, cls, clsn, bmax, p32, scales_k, blk_begin, blk_end, scores, gkey, \
+                             st);
 #define FATHOM_SCAN_CASE4(GG)                    \
   case GG:                                       \
     if (tpl == 32) { FATHOM_SCAN_LAUNCH(GG, 32) } \
@@ -525,14 +547,13 @@ int scan_dispatch(const float* q, int64_t BH, int G, int64_t n, int64_t sub, con
 extern "C" int fathom_scan(const float* q, int64_t BH, int G, int64_t n, int64_t sub, const int32_t* cls,
                            const int32_t* clsn, int bmax, const uint64_t* planes_k, const uint16_t* scales_k,
                            int64_t blk_begin, int64_t blk_end, float* scores, void* stream) {
-  return scan_dispatch(q, BH, G, n, sub, cls, clsn, bmax, planes_k, scales_k, blk_begin, blk_end, scores,
+  return scan_dispatch(q, BH, G, n, sub, cls, clsn, bmax, planes_k, scales_k, blk_begin, blk_end, scores, nullptr,
                        reinterpret_cast<cudaStream_t>(stream));
 }
 
 extern "C" size_t fathom_scan_select_workspace_bytes(int64_t BH, int G, int64_t n, int64_t kk) {
-  (void)n;
   (void)kk;
-  return BH > 0 && G > 0 ? selectk::ws_bytes(BH * G) : 0;
+  return BH > 0 && G > 0 && n > 0 ? selectk::select_ws_bytes(BH * G, n) : 0;
 }
 
 extern "C" int fathom_scan_select(const float* q, int64_t BH, int G, int64_t n, int64_t sub, const int32_t* cls,
@@ -547,19 +568,23 @@ extern "C" int fathom_scan_select(const float* q, int64_t BH, int G, int64_t n, 
                  "scan_select: kk=%lld outside 1..min(4096, n=%lld)", (long long)kk, (long long)n);
   FATHOM_REQUIRE(append_sink >= 0 && append_local >= 0 && out_stride >= kk + append_sink + append_local,
                  FATHOM_ERR_SHAPE, "scan_select: bad output stride");
-  FATHOM_REQUIRE(workspace_bytes >= selectk::ws_bytes(rows) && (reinterpret_cast<uintptr_t>(workspace) & 255) == 0,
-                 FATHOM_ERR_WORKSPACE, "scan_select: workspace needs %zu bytes, 256-byte aligned",
-                 selectk::ws_bytes(rows));
+  FATHOM_REQUIRE((reinterpret_cast<uintptr_t>(workspace) & 255) == 0, FATHOM_ERR_WORKSPACE,
+                 "scan_select: workspace must be 256-byte aligned");
+  // the group-key selection takes its keys from the scan's epilogue
+  const bool gkeys = selectk::group_select_applies(rows, n, kk, mask_lo, mask_hi, workspace_bytes);
+  FATHOM_REQUIRE(gkeys || workspace_bytes >= selectk::ws_bytes(rows), FATHOM_ERR_WORKSPACE,
+                 "scan_select: workspace needs %zu bytes (got %zu)", selectk::select_ws_bytes(rows, n), workspace_bytes);
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   const int64_t nblk = cdiv(n, BLK);
-  int r = scan_dispatch(q, BH, G, n, sub, cls, clsn, bmax, planes_k, scales_k, 0, nblk, scores, st);
+  int r = scan_dispatch(q, BH, G, n, sub, cls, clsn, bmax, planes_k, scales_k, 0, nblk, scores,
+                        gkeys ? static_cast<uint32_t*>(workspace) : nullptr, st);
   if (r != FATHOM_OK) return r;
   if (scan_done_event) {
     const cudaError_t e = cudaEventRecord(reinterpret_cast<cudaEvent_t>(scan_done_event), st);
     if (e != cudaSuccess) return set_error(FATHOM_ERR_CUDA, "scan_select: event record: %s", cudaGetErrorString(e));
   }
   return selectk::launch_select(scores, rows, n, n, kk, mask_lo, mask_hi, index_offset, out_idx, out_stride,
-                                out_scores, append_sink, append_local, workspace, workspace_bytes, st);
+                                out_scores, append_sink, append_local, workspace, workspace_bytes, gkeys, st);
 }
 
 extern "C" int fathom_wait_timeouts(unsigned long long* count, int reset) {

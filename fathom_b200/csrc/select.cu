@@ -306,6 +306,37 @@ __device__ uint64_t bitonic_desc_regs(uint64_t v, int P, uint64_t* s_x) {
   return v;
 }
 
+// Sorts the kk selected candidates of s_sel (descending: score desc, index asc) and writes the row's
+// output: indices (+ index_offset), optional scores, then the appended sink and local indices.
+// s_sel holds next_pow2(kk) entries; s_x is scratch of as many.
+__device__ void write_sorted(uint64_t* s_sel, uint64_t* s_x, int64_t row, int64_t n, int64_t kk, int64_t index_offset,
+                             int64_t* __restrict__ out_idx, int64_t out_stride, float* __restrict__ out_scores,
+                             int64_t append_sink, int64_t append_local) {
+  const int P = next_pow2((int)kk);
+  int64_t* o = out_idx + row * out_stride;
+  if (P <= (int)blockDim.x) {
+    // one value per thread, sorted in registers
+    uint64_t v = threadIdx.x < kk ? s_sel[threadIdx.x] : 0ull;
+    __syncthreads();
+    v = bitonic_desc_regs(v, P, s_x);
+    if (threadIdx.x < kk) {
+      o[threadIdx.x] = (int64_t)(uint32_t)(~(uint32_t)v) + index_offset;
+      if (out_scores) out_scores[row * kk + threadIdx.x] = key2f((uint32_t)(v >> 32));
+    }
+  } else {
+    for (int i = (int)kk + threadIdx.x; i < P; i += blockDim.x) s_sel[i] = 0ull;
+    __syncthreads();
+    bitonic_desc(s_sel, P);
+    for (int i = threadIdx.x; i < kk; i += blockDim.x) {
+      const uint64_t v = s_sel[i];
+      o[i] = (int64_t)(uint32_t)(~(uint32_t)v) + index_offset;
+      if (out_scores) out_scores[row * kk + i] = key2f((uint32_t)(v >> 32));
+    }
+  }
+  for (int64_t i = threadIdx.x; i < append_sink; i += blockDim.x) o[kk + i] = i;
+  for (int64_t i = threadIdx.x; i < append_local; i += blockDim.x) o[kk + append_sink + i] = n - append_local + i;
+}
+
 __global__ void __launch_bounds__(FT) finalize_kernel(const float* __restrict__ scores, int64_t n, int64_t row_stride,
                                                       int64_t kk, int64_t mask_lo, int64_t mask_hi,
                                                       const uint32_t* __restrict__ count,
@@ -357,29 +388,7 @@ __global__ void __launch_bounds__(FT) finalize_kernel(const float* __restrict__ 
     exact_select_row(scores + row * row_stride, n, kk, mask_lo, mask_hi, s_sel, s_hist, s_part, &s_res, s_warp,
                      &s_cnt);
   }
-  const int P = next_pow2((int)kk);
-  int64_t* o = out_idx + row * out_stride;
-  if (P <= FT) {
-    // one value per thread, sorted in registers
-    uint64_t v = threadIdx.x < kk ? s_sel[threadIdx.x] : 0ull;
-    __syncthreads();
-    v = bitonic_desc_regs(v, P, s_buf);
-    if (threadIdx.x < kk) {
-      o[threadIdx.x] = (int64_t)(uint32_t)(~(uint32_t)v) + index_offset;
-      if (out_scores) out_scores[row * kk + threadIdx.x] = key2f((uint32_t)(v >> 32));
-    }
-  } else {
-    for (int i = (int)kk + threadIdx.x; i < P; i += blockDim.x) s_sel[i] = 0ull;
-    __syncthreads();
-    bitonic_desc(s_sel, P);
-    for (int i = threadIdx.x; i < kk; i += blockDim.x) {
-      const uint64_t v = s_sel[i];
-      o[i] = (int64_t)(uint32_t)(~(uint32_t)v) + index_offset;
-      if (out_scores) out_scores[row * kk + i] = key2f((uint32_t)(v >> 32));
-    }
-  }
-  for (int64_t i = threadIdx.x; i < append_sink; i += blockDim.x) o[kk + i] = i;
-  for (int64_t i = threadIdx.x; i < append_local; i += blockDim.x) o[kk + append_sink + i] = n - append_local + i;
+  write_sorted(s_sel, s_buf, row, n, kk, index_offset, out_idx, out_stride, out_scores, append_sink, append_local);
 }
 
 __global__ void __launch_bounds__(FT) merge_kernel(const float* __restrict__ cs, const int64_t* __restrict__ ci,
@@ -442,6 +451,221 @@ __global__ void __launch_bounds__(FT) merge_kernel(const float* __restrict__ cs,
   }
 }
 
+// ---------------------------------------------------------------------------------------------
+// Group-maximum selection (see select_common.cuh).
+
+// One thread per group of GROUP scores: the largest key of the group (keys, not floats, so -0 and
+// +0 order as the selection orders them).
+__global__ void __launch_bounds__(256) gmax_kernel(const float* __restrict__ scores, int64_t n, int64_t row_stride,
+                                                   int64_t ng, uint32_t* __restrict__ gkey) {
+  const int64_t row = blockIdx.y;
+  const int64_t g = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (g >= ng) return;
+  const float* r = scores + row * row_stride;
+  const int64_t t0 = g * GROUP, t1 = t0 + GROUP < n ? t0 + GROUP : n;
+  uint32_t m = 0;
+  if (t1 - t0 == GROUP && (reinterpret_cast<uintptr_t>(r + t0) & 15) == 0) {
+#pragma unroll
+    for (int u = 0; u < GROUP / 4; ++u) {
+      const float4 v = __ldg(reinterpret_cast<const float4*>(r + t0) + u);
+      m = max(m, max(max(f2key(v.x), f2key(v.y)), max(f2key(v.z), f2key(v.w))));
+    }
+  } else {
+    for (int64_t i = t0; i < t1; ++i) m = max(m, f2key(r[i]));
+  }
+  gkey[row * ng + g] = m;
+}
+
+constexpr int QT = 1024;   // threads of the group-selection CTA
+
+// One CTA per row.
+//   1 histogram of the top 12 key bits of the fully unmasked groups' keys (warp-aggregated shared
+//     atomics); tau = lower edge of the boundary bin, so at least kk unmasked tokens have key >= tau
+//   2 list the groups whose key reaches tau, read their scores, keep every token with key >= tau
+//     (masked tokens carry the key of -inf, as in the histogram path) as a candidate
+//   3 radix-refine the candidates to exactly kk, sort, write.
+// More than CAP listed groups or candidates (massive ties) takes the exact whole-row selection.
+__global__ void __launch_bounds__(QT) gsel_kernel(const float* __restrict__ scores, int64_t n, int64_t row_stride,
+                                                  int64_t kk, int64_t mask_lo, int64_t mask_hi,
+                                                  const uint32_t* __restrict__ gkey, int64_t ng, int64_t index_offset,
+                                                  int64_t* __restrict__ out_idx, int64_t out_stride,
+                                                  float* __restrict__ out_scores, int64_t append_sink,
+                                                  int64_t append_local) {
+  extern __shared__ uint64_t s_dyn[];  // CAP candidates, then MAX_KK selected (the group list before that)
+  uint64_t* s_buf = s_dyn;
+  uint64_t* s_sel = s_dyn + CAP;
+  int32_t* s_glist = reinterpret_cast<int32_t*>(s_sel);   // CAP group ids; phase 2 only
+  __shared__ uint32_t s_hist[NBINS];
+  __shared__ uint32_t s_part[QT];
+  __shared__ uint32_t s_warp[33];
+  __shared__ uint32_t s_ctl[4];
+  __shared__ uint32_t s_cnt, s_nq;
+  __shared__ int s_res;
+  const int64_t row = blockIdx.x;
+  const int tid = threadIdx.x, lane = tid & 31;
+  const uint32_t* gk = gkey + row * ng;
+  const float* r = scores + row * row_stride;
+  const int64_t lo = mask_lo < 0 ? 0 : (mask_lo > n ? n : mask_lo);
+  const int64_t hi = mask_hi < 0 ? 0 : (mask_hi > n ? n : mask_hi);
+  const int64_t g_lo = (lo + GROUP - 1) / GROUP;
+  const int64_t g_hi = hi == n ? ng : hi / GROUP;
+  for (int b = tid; b < NBINS; b += QT) s_hist[b] = 0;
+  if (tid == 0) {
+    s_cnt = 0;
+    s_nq = 0;
+  }
+  __syncthreads();
+
+  // 1: histogram of the unmasked groups' keys
+  constexpr int U = 8;
+  for (int64_t base = 0; base < ng; base += (int64_t)QT * U) {
+    uint32_t bin[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int64_t g = base + (int64_t)u * QT + tid;
+      bin[u] = (g >= g_lo && g < g_hi) ? (__ldg(gk + g) >> (32 - HBITS)) : (uint32_t)NBINS;
+    }
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const uint32_t peers = __match_any_sync(0xffffffffu, bin[u]);
+      if (bin[u] < (uint32_t)NBINS && lane == __ffs(peers) - 1) atomicAdd(&s_hist[bin[u]], (uint32_t)__popc(peers));
+    }
+  }
+  __syncthreads();
+  if (tid < 32) {
+    uint32_t above;
+    const int b = warp_boundary_bin_smem(s_hist, kk, &above);   // 0 when fewer than kk groups: all qualify
+    if (tid == 0) s_ctl[0] = (uint32_t)b;
+  }
+  __syncthreads();
+  const uint32_t tau = s_ctl[0] << (32 - HBITS);
+
+  // 2a: the groups whose key reaches tau, in a shared list
+  for (int64_t base = 0; base < ng; base += (int64_t)QT * U) {
+    uint32_t q = 0;
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int64_t g = base + (int64_t)u * QT + tid;
+      if (g < ng && __ldg(gk + g) >= tau) q |= 1u << u;
+    }
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const bool take = (q >> u) & 1u;
+      const uint32_t m = __ballot_sync(0xffffffffu, take);
+      if (m) {
+        uint32_t pos0 = 0;
+        if (lane == 0) pos0 = atomicAdd(&s_nq, (uint32_t)__popc(m));
+        pos0 = __shfl_sync(0xffffffffu, pos0, 0);
+        const uint32_t pos = pos0 + __popc(m & ((1u << lane) - 1));
+        if (take && pos < (uint32_t)CAP) s_glist[pos] = (int32_t)(base + (int64_t)u * QT + tid);
+      }
+    }
+  }
+  __syncthreads();
+  const uint32_t nq = s_nq;
+
+  // 2b: one listed group per thread; its tokens with key >= tau become candidates
+  if (nq <= (uint32_t)CAP) {
+    for (uint32_t jb = 0; jb < nq; jb += QT) {
+      const uint32_t j = jb + tid;
+      uint32_t take = 0;
+      int64_t t0 = 0;
+      if (j < nq) {
+        t0 = (int64_t)s_glist[j] * GROUP;
+        const int64_t t1 = t0 + GROUP < n ? t0 + GROUP : n;
+        const bool inside = t0 >= lo && t1 <= hi;
+        if (t1 - t0 == GROUP && (reinterpret_cast<uintptr_t>(r + t0) & 15) == 0) {
+#pragma unroll
+          for (int u = 0; u < GROUP / 4; ++u) {
+            const float4 v = __ldg(reinterpret_cast<const float4*>(r + t0) + u);
+            const float e[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+              const int64_t i = t0 + 4 * u + c;
+              const uint32_t key = (inside || (i >= lo && i < hi)) ? f2key(e[c]) : KEY_NEG_INF;
+              if (key >= tau) take |= 1u << (4 * u + c);
+            }
+          }
+        } else {
+          for (int64_t i = t0; i < t1; ++i) {
+            const uint32_t key = (i >= lo && i < hi) ? f2key(r[i]) : KEY_NEG_INF;
+            if (key >= tau) take |= 1u << (int)(i - t0);
+          }
+        }
+      }
+      // warp-aggregated reservation of the candidate slots
+      const uint32_t c = (uint32_t)__popc(take);
+      uint32_t incl = c;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const uint32_t y = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += y;
+      }
+      uint32_t base = 0;
+      if (lane == 31) base = atomicAdd(&s_cnt, incl);
+      base = __shfl_sync(0xffffffffu, base, 31);
+      uint32_t pos = base + incl - c;
+      while (take) {
+        const int b = __ffs(take) - 1;
+        take &= take - 1;
+        const int64_t i = t0 + b;
+        const uint32_t key = (i >= lo && i < hi) ? f2key(r[i]) : KEY_NEG_INF;
+        if (pos < (uint32_t)CAP) s_buf[pos] = ((uint64_t)key << 32) | (uint32_t)(~(uint32_t)i);
+        ++pos;
+      }
+    }
+  }
+  __syncthreads();
+  const uint32_t cnt = s_cnt;
+
+  if (nq <= (uint32_t)CAP && cnt <= (uint32_t)CAP && cnt >= (uint32_t)kk) {
+    // 3: exactly kk of the candidates (at least kk of them exist, all distinct)
+    for (int b = tid; b < NBINS; b += QT) s_hist[b] = 0;
+    __syncthreads();
+    for (int i = tid; i < (int)cnt; i += QT) atomicAdd(&s_hist[s_buf[i] >> 52], 1u);
+    __syncthreads();
+    if (tid < 32) {
+      uint32_t above;
+      const int b = warp_boundary_bin_smem(s_hist, kk, &above);
+      if (tid == 0) {
+        s_ctl[1] = (uint32_t)b;
+        s_ctl[2] = above;
+      }
+    }
+    __syncthreads();
+    const uint32_t top12 = s_ctl[1];
+    const int64_t need = kk - (int64_t)s_ctl[2];
+    __syncthreads();
+    const uint64_t C = refine_threshold(s_buf, (int)cnt, top12, need, s_hist, s_ctl);
+    if (tid == 0) s_cnt = 0;
+    __syncthreads();
+    for (int i = tid; i < (int)cnt; i += QT)
+      if (s_buf[i] >= C) {
+        const uint32_t pos = atomicAdd(&s_cnt, 1u);
+        if (pos < (uint32_t)MAX_KK) s_sel[pos] = s_buf[i];
+      }
+    __syncthreads();
+  } else {
+    exact_select_row(r, n, kk, mask_lo, mask_hi, s_sel, s_hist, s_part, &s_res, s_warp, &s_cnt);
+  }
+  write_sorted(s_sel, s_buf, row, n, kk, index_offset, out_idx, out_stride, out_scores, append_sink, append_local);
+}
+
+int run_group_select(const float* scores, int64_t rows, int64_t n, int64_t row_stride, int64_t kk, int64_t mask_lo,
+                     int64_t mask_hi, int64_t index_offset, int64_t* out_idx, int64_t out_stride, float* out_scores,
+                     int64_t append_sink, int64_t append_local, uint32_t* gkey, bool gkeys_ready, cudaStream_t st) {
+  const int64_t ng = n_groups(n);
+  if (!gkeys_ready) {
+    dim3 grid((unsigned)cdiv(ng, 256), (unsigned)rows);
+    gmax_kernel<<<grid, 256, 0, st>>>(scores, n, row_stride, ng, gkey);
+  }
+  const size_t smem = (CAP + MAX_KK) * sizeof(uint64_t);
+  cudaFuncSetAttribute(gsel_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  gsel_kernel<<<(unsigned)rows, QT, smem, st>>>(scores, n, row_stride, kk, mask_lo, mask_hi, gkey, ng, index_offset,
+                                                 out_idx, out_stride, out_scores, append_sink, append_local);
+  return check_launch("select_topk (group keys)");
+}
+
 // collect + finalize on a histogram and boundary bins already built
 int select_tail(const float* scores, int64_t rows, int64_t n, int64_t row_stride, int64_t kk, int64_t mask_lo,
                        int64_t mask_hi, int64_t index_offset, int64_t* out_idx, int64_t out_stride,
@@ -460,7 +684,8 @@ int select_tail(const float* scores, int64_t rows, int64_t n, int64_t row_stride
 
 int run_select(const float* scores, int64_t rows, int64_t n, int64_t row_stride, int64_t kk, int64_t mask_lo,
                int64_t mask_hi, int64_t index_offset, int64_t* out_idx, int64_t out_stride, float* out_scores,
-               int64_t append_sink, int64_t append_local, void* workspace, size_t workspace_bytes, cudaStream_t st) {
+               int64_t append_sink, int64_t append_local, void* workspace, size_t workspace_bytes, bool gkeys_ready,
+               cudaStream_t st) {
   FATHOM_REQUIRE(scores && out_idx, FATHOM_ERR_NULL, "select_topk: NULL pointer");
   FATHOM_REQUIRE(rows >= 1 && rows <= 65535 && n >= 1 && n <= 0xffffffffLL, FATHOM_ERR_SHAPE,
                  "select_topk: need 1 <= rows <= 65535 and 1 <= n < 2^32");
@@ -469,9 +694,14 @@ int run_select(const float* scores, int64_t rows, int64_t n, int64_t row_stride,
   FATHOM_REQUIRE(row_stride >= n && out_stride >= kk + append_sink + append_local, FATHOM_ERR_SHAPE,
                  "select_topk: bad strides");
   FATHOM_REQUIRE(workspace != nullptr, FATHOM_ERR_NULL, "select_topk: workspace is NULL");
-  FATHOM_REQUIRE(workspace_bytes >= ws_bytes(rows) && (reinterpret_cast<uintptr_t>(workspace) & 255) == 0,
-                 FATHOM_ERR_WORKSPACE, "select_topk: workspace needs %zu bytes, 256-byte aligned (got %zu)",
-                 ws_bytes(rows), workspace_bytes);
+  FATHOM_REQUIRE((reinterpret_cast<uintptr_t>(workspace) & 255) == 0, FATHOM_ERR_WORKSPACE,
+                 "select_topk: workspace must be 256-byte aligned");
+  if (group_select_applies(rows, n, kk, mask_lo, mask_hi, workspace_bytes))
+    return run_group_select(scores, rows, n, row_stride, kk, mask_lo, mask_hi, index_offset, out_idx, out_stride,
+                            out_scores, append_sink, append_local, static_cast<uint32_t*>(workspace), gkeys_ready, st);
+  FATHOM_REQUIRE(!gkeys_ready, FATHOM_ERR_UNSUPPORTED, "select_topk: group keys given where they do not apply");
+  FATHOM_REQUIRE(workspace_bytes >= ws_bytes(rows), FATHOM_ERR_WORKSPACE,
+                 "select_topk: workspace needs %zu bytes (got %zu)", select_ws_bytes(rows, n), workspace_bytes);
   Workspace w = carve(workspace, rows);
   cudaError_t e = cudaMemsetAsync(workspace, 0, zeroed_bytes(rows), st);
   if (e != cudaSuccess) return set_error(FATHOM_ERR_CUDA, "select_topk: memset: %s", cudaGetErrorString(e));
@@ -488,9 +718,9 @@ namespace selectk {
 int launch_select(const float* scores, int64_t rows, int64_t n, int64_t row_stride, int64_t kk, int64_t mask_lo,
                   int64_t mask_hi, int64_t index_offset, int64_t* out_idx, int64_t out_stride, float* out_scores,
                   int64_t append_sink, int64_t append_local, void* workspace, size_t workspace_bytes,
-                  cudaStream_t st) {
+                  bool gkeys_ready, cudaStream_t st) {
   return run_select(scores, rows, n, row_stride, kk, mask_lo, mask_hi, index_offset, out_idx, out_stride, out_scores,
-                    append_sink, append_local, workspace, workspace_bytes, st);
+                    append_sink, append_local, workspace, workspace_bytes, gkeys_ready, st);
 }
 
 }  // namespace selectk
@@ -499,9 +729,8 @@ int launch_select(const float* scores, int64_t rows, int64_t n, int64_t row_stri
 using namespace fathom;
 
 extern "C" size_t fathom_select_workspace_bytes(int64_t rows, int64_t n, int64_t kk) {
-  (void)n;
   (void)kk;
-  return rows > 0 ? ws_bytes(rows) : 0;
+  return rows > 0 && n > 0 ? select_ws_bytes(rows, n) : 0;
 }
 
 extern "C" int fathom_select_topk(const float* scores, int64_t rows, int64_t n, int64_t row_stride, int64_t kk,
@@ -509,7 +738,7 @@ extern "C" int fathom_select_topk(const float* scores, int64_t rows, int64_t n, 
                                   int64_t out_stride, float* out_scores, void* workspace, size_t workspace_bytes,
                                   void* stream) {
   return run_select(scores, rows, n, row_stride, kk, mask_lo, mask_hi, index_offset, out_idx, out_stride, out_scores,
-                    0, 0, workspace, workspace_bytes, reinterpret_cast<cudaStream_t>(stream));
+                    0, 0, workspace, workspace_bytes, false, reinterpret_cast<cudaStream_t>(stream));
 }
 
 extern "C" int fathom_sink_local_topk(const float* scores, int64_t rows, int64_t n, int64_t k, int64_t sink,
@@ -520,7 +749,7 @@ extern "C" int fathom_sink_local_topk(const float* scores, int64_t rows, int64_t
                  (long long)sink, (long long)local);
   FATHOM_REQUIRE(local <= n && sink <= n, FATHOM_ERR_SHAPE, "sink_local_topk: sink/local exceed n");
   return run_select(scores, rows, n, n, k - sink - local, sink, n - local, 0, idx, k, nullptr, sink, local, workspace,
-                    workspace_bytes, reinterpret_cast<cudaStream_t>(stream));
+                    workspace_bytes, false, reinterpret_cast<cudaStream_t>(stream));
 }
 
 extern "C" int fathom_merge_topk(const float* cand_scores, const int64_t* cand_idx, int64_t rows, int64_t m, int64_t kk,

@@ -1,4 +1,4 @@
-// Internal: shared by select.cu and scan.cu (the fused scan + selection histogram).
+// Internal: shared by select.cu and scan.cu (the scan writes the selection's group keys).
 #pragma once
 #include "common.cuh"
 
@@ -30,6 +30,31 @@ constexpr size_t zeroed_bytes(int64_t rows) {
 
 constexpr size_t ws_bytes(int64_t rows) {
   return zeroed_bytes(rows) + align256(rows * sizeof(uint32_t)) + align256(rows * (size_t)CAP * sizeof(uint64_t));
+}
+
+// Group-maximum selection: one key per GROUP consecutive tokens of a row (the order-preserving key
+// of the group's largest score), written by the scan's epilogue or by a pass over the scores.
+// If at least kk groups have a key >= tau, at least kk distinct tokens do, so the boundary bin of
+// the group keys bounds the kk-th largest token key from below; only the groups whose key reaches
+// it are read again.  Used when the fully unmasked groups number at least 2 * kk.
+constexpr int GROUP = 32;
+constexpr int64_t n_groups(int64_t n) { return (n + GROUP - 1) / GROUP; }
+constexpr size_t gkey_bytes(int64_t rows, int64_t n) { return align256(rows * n_groups(n) * sizeof(uint32_t)); }
+// Workspace that serves both selection paths.
+constexpr size_t select_ws_bytes(int64_t rows, int64_t n) {
+  return ws_bytes(rows) > gkey_bytes(rows, n) ? ws_bytes(rows) : gkey_bytes(rows, n);
+}
+// Groups lying entirely inside the unmasked range [mask_lo, mask_hi) of a row of n tokens.
+inline int64_t unmasked_groups(int64_t n, int64_t mask_lo, int64_t mask_hi) {
+  const int64_t lo = mask_lo < 0 ? 0 : (mask_lo > n ? n : mask_lo);
+  const int64_t hi = mask_hi < 0 ? 0 : (mask_hi > n ? n : mask_hi);
+  const int64_t g_lo = (lo + GROUP - 1) / GROUP;
+  const int64_t g_hi = hi == n ? n_groups(n) : hi / GROUP;
+  return g_hi > g_lo ? g_hi - g_lo : 0;
+}
+inline bool group_select_applies(int64_t rows, int64_t n, int64_t kk, int64_t mask_lo, int64_t mask_hi,
+                                 size_t workspace_bytes) {
+  return unmasked_groups(n, mask_lo, mask_hi) >= 2 * kk && workspace_bytes >= gkey_bytes(rows, n);
 }
 
 inline Workspace carve(void* base, int64_t rows) {
@@ -183,11 +208,12 @@ static __device__ int warp_boundary_bin_smem(const uint32_t* hist, int64_t kk, u
   return m ? __shfl_sync(0xffffffffu, found, src) : 0;
 }
 
-// The whole selection over score rows (workspace memset, histogram, collect, finalize): see select.cu.
+// The whole selection over score rows: see select.cu.  With gkeys_ready the group keys are already in
+// the workspace (written by the scan) and group_select_applies() held for these arguments.
 int launch_select(const float* scores, int64_t rows, int64_t n, int64_t row_stride, int64_t kk, int64_t mask_lo,
                   int64_t mask_hi, int64_t index_offset, int64_t* out_idx, int64_t out_stride, float* out_scores,
                   int64_t append_sink, int64_t append_local, void* workspace, size_t workspace_bytes,
-                  cudaStream_t st);
+                  bool gkeys_ready, cudaStream_t st);
 
 }  // namespace selectk
 }  // namespace fathom

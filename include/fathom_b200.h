@@ -107,17 +107,20 @@ int fathom_scan(const float* q, int64_t BH, int G, int64_t n, int64_t sub, const
  *   count may be NULL; reset != 0 zeroes the counter after reading it. */
 int fathom_wait_timeouts(unsigned long long* count, int reset);
 
-/* Workspace bytes of fathom_scan_select. */
+/* Workspace bytes of fathom_scan_select: enough for either selection path (below). */
 size_t fathom_scan_select_workspace_bytes(int64_t BH, int G, int64_t n, int64_t kk);
 
 /* PlaneStore.scan followed by sink_local_topk-style selection in one call (kernels/bitplane.py:319-338,
- * 372-378): the scan, then the selection's histogram / collect / finalize passes, all on the stream.
- * Writes scores [BH][G][n] (all blocks) and, per row r = bh*G+g, the top-kk of tokens in
- * [mask_lo, mask_hi) plus index_offset to out_idx [r][out_stride] in (score desc, index asc) order,
- * followed by 0..append_sink-1 and n-append_local..n-1; the selected scores to out_scores [r][kk] if
- * not NULL.  sink_local_topk(k, sink, local) is kk = k-sink-local, mask [sink, n-local), offset 0,
- * append (sink, local), out_stride k.  scan_done_event (a cudaEvent_t, may be NULL) is recorded on
- * the stream right after the scan kernel, to time the scan alone. */
+ * 372-378), all on the stream.  Writes scores [BH][G][n] (all blocks) and, per row r = bh*G+g, the
+ * top-kk of tokens in [mask_lo, mask_hi) plus index_offset to out_idx [r][out_stride] in (score desc,
+ * index asc) order, followed by 0..append_sink-1 and n-append_local..n-1; the selected scores to
+ * out_scores [r][kk] if not NULL.  sink_local_topk(k, sink, local) is kk = k-sink-local, mask
+ * [sink, n-local), offset 0, append (sink, local), out_stride k.  When the row has at least 2*kk
+ * fully unmasked 32-token groups, the scan also writes each group's largest score key to the
+ * workspace and one selection kernel per row works from those (group-key path); otherwise the
+ * histogram / collect / finalize passes run.  The workspace must hold the chosen path's buffers;
+ * fathom_scan_select_workspace_bytes() covers both.  scan_done_event (a cudaEvent_t, may be NULL)
+ * is recorded on the stream right after the scan kernel, to time the scan alone. */
 int fathom_scan_select(const float* q, int64_t BH, int G, int64_t n, int64_t sub, const int32_t* cls,
                        const int32_t* clsn, int bmax, const uint64_t* planes_k, const uint16_t* scales_k, int64_t kk,
                        int64_t mask_lo, int64_t mask_hi, int64_t index_offset, int64_t append_sink,
@@ -126,7 +129,9 @@ int fathom_scan_select(const float* q, int64_t BH, int G, int64_t n, int64_t sub
 
 /* ---------------------------------------------------------------- selection */
 
-/* Workspace bytes fathom_select_topk / fathom_sink_local_topk need for `rows` rows. */
+/* Workspace bytes fathom_select_topk / fathom_sink_local_topk need for `rows` rows of n scores:
+ * enough for either selection path (the group-key path, taken when a row has at least 2*kk fully
+ * unmasked 32-token groups and the workspace holds rows * ceil(n/32) keys; else the histogram path). */
 size_t fathom_select_workspace_bytes(int64_t rows, int64_t n, int64_t kk);
 
 /* Top-kk of each row of scores [rows][n] (row r at scores + r*row_stride), with tokens

@@ -38,8 +38,9 @@ def test_null_and_shape_errors_are_status_codes():
     assert L.fathom_make_plan(p, p, 4, 5, 30, p, p, p, p, p, p, p, None) == _lib.FATHOM_ERR_SHAPE
     assert L.fathom_sink_local_topk(p, 1, 100, 10, 4, 6, p, p, 1 << 20, None) == _lib.FATHOM_ERR_SHAPE
     need = L.fathom_select_workspace_bytes(4, 1000, 10)
-    assert need > 0
-    assert L.fathom_select_topk(p, 4, 1000, 1000, 10, 0, 1000, 0, p, 10, None, ctypes.c_void_p(256), need - 1,
+    assert need >= 512
+    # 256 bytes hold neither the group keys (4 rows x 32 groups) nor the histogram path's buffers
+    assert L.fathom_select_topk(p, 4, 1000, 1000, 10, 0, 1000, 0, p, 10, None, ctypes.c_void_p(256), 256,
                                 None) == _lib.FATHOM_ERR_WORKSPACE
     assert L.fathom_merge_topk(p, p, 1, 9000, 10, p, None, None) == _lib.FATHOM_ERR_SHAPE
     assert L.fathom_decode_attention(p, 2, 4, p, 20000, p, p, 10, 0, 10, None, None, 0, p, None, p, 1 << 30,

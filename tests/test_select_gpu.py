@@ -163,3 +163,53 @@ def test_scan_topk_all_ties():
     plan = bp.make_plan(d["g"].cuda(), 0.0)
     got = bp.scan_topk(st, d["q"].cuda(), plan, 580, 4, 64).cpu().numpy()
     assert np.array_equal(got, O.sink_local_topk(np.zeros((2, 4, 30000), np.float32), 580, 4, 64))
+
+
+def _hist_path_bytes(rows):
+    a = lambda x: (x + 255) // 256 * 256
+    return a(rows * 4096 * 4) + 3 * a(rows * 4) + a(rows * 8192 * 8)
+
+
+@pytest.mark.parametrize("sink,local,kk", [(0, 0, 500), (4, 64, 508), (5, 33, 4000), (100, 1000, 64)])
+def test_group_path_equals_histogram_path(sink, local, kk):
+    """The group-key selection (a workspace that holds the group keys) and the histogram selection
+    (a workspace sized for the histogram path only) give the oracle's exact output."""
+    import ctypes
+    from fathom_b200 import _lib
+    rows, n = 2, (1 << 20) + 77
+    g = torch.Generator().manual_seed(kk + sink)
+    s = torch.randn(rows, n, generator=g)
+    s[:, 5000:5010] = 3.0                  # a few exact ties near the top
+    sd = s.cuda()
+    k = kk + sink + local
+    full = _lib.lib().fathom_select_workspace_bytes(rows, n, kk)
+    small = _hist_path_bytes(rows)
+    assert full > small                    # the group keys need more than the histogram path
+    outs = []
+    for nbytes in (full, small):
+        ws = torch.empty(nbytes, dtype=torch.uint8, device="cuda")
+        idx = torch.empty(rows, k, dtype=torch.int64, device="cuda")
+        _lib.check(_lib.lib().fathom_sink_local_topk(_lib.ptr(sd), rows, n, k, sink, local, _lib.ptr(idx), _lib.ptr(ws),
+                                                     ctypes.c_size_t(nbytes), None), "sink_local_topk")
+        outs.append(idx.cpu().numpy())
+    ref = O.sink_local_topk(s.numpy(), k, sink, local)
+    assert np.array_equal(outs[0], ref) and np.array_equal(outs[1], ref)
+
+
+@pytest.mark.parametrize("n", [31, 32, 33, 64 * 37 + 5, 40000])
+def test_group_path_ragged_rows(n):
+    """Rows whose length is not a multiple of the 32-token group, masks that cut groups, scan-written
+    group keys (fused) against the oracle."""
+    from fathom_b200 import bitplane as bp
+    from fathom_b200.synth import make_layer
+    d = make_layer(2, 4, n, seed=n, with_v=False)
+    st = bp.PlaneStore(d["K"].cuda())
+    plan = bp.make_plan(d["g"].cuda(), 48.0)
+    q = d["q"].cuda()
+    kk = max(1, min(300, n // 70))
+    lo, hi = 3, n - 7 if n > 20 else n
+    idx, vals, s = bp.scan_select(st, q, plan, kk, mask_lo=lo, mask_hi=hi, with_scores=True)
+    m = s.cpu().numpy().copy()
+    m[..., :lo] = -np.inf
+    m[..., hi:] = -np.inf
+    assert np.array_equal(idx.cpu().numpy(), O.topk_desc(m, kk))
