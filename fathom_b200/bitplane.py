@@ -106,6 +106,23 @@ def bytes_planes(t, n):
 
 
 # ------------------------------------------------------------------ plan
+_BUDGETS = {}
+
+
+def _budget_tensor(value, BH, dev):
+    """A [BH] fp32 tensor holding a scalar budget, kept per (device, BH, value) so a decode loop does not
+    launch a fill kernel per call; made fresh while a CUDA graph is being captured (the graph then owns it)."""
+    if torch.cuda.is_current_stream_capturing():
+        return torch.full((BH,), value, device=dev)
+    key = (dev.index if dev.index is not None else torch.cuda.current_device(), BH, value)
+    t = _BUDGETS.get(key)
+    if t is None:
+        if len(_BUDGETS) > 256:
+            _BUDGETS.clear()
+        t = _BUDGETS[key] = torch.full((BH,), value, device=dev)
+    return t
+
+
 def make_plan(g, budget, bmax=4, iters=30):
     """g [BH, D] fp32 group-summed gain q_j^2 Var(k_j); budget scalar or [BH] (bits per token).
     Returns dict of device tensors t int8 [BH,D], pairs int32 [BH,D*bmax], npairs [BH], act [BH,D],
@@ -116,7 +133,7 @@ def make_plan(g, budget, bmax=4, iters=30):
         raise ValueError(f"make_plan: g must be [BH, {D}]")
     dev = g.device
     if not torch.is_tensor(budget):
-        budget = torch.full((BH,), float(budget), device=dev)
+        budget = _budget_tensor(float(budget), BH, dev)
     budget = budget.to(device=dev, dtype=torch.float32).reshape(-1).expand(BH).contiguous()
     gc = g.contiguous().float()
     t = torch.empty(BH, d, dtype=torch.int8, device=dev)

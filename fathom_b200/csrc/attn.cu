@@ -109,12 +109,18 @@ __global__ void __launch_bounds__(DT) dedupe_kernel(const int64_t* __restrict__ 
   __syncthreads();
   const int64_t* ib = idx + bh * M;
   int pos[PICKS_PER_THREAD];
+  int64_t tv[PICKS_PER_THREAD];   // every pick load in flight before the first insert
+#pragma unroll
+  for (int u = 0; u < PICKS_PER_THREAD; ++u) {
+    const int64_t i = threadIdx.x + (int64_t)u * DT;
+    tv[u] = i < M ? ib[i] : -1;
+  }
 #pragma unroll
   for (int u = 0; u < PICKS_PER_THREAD; ++u) {
     const int64_t i = threadIdx.x + (int64_t)u * DT;
     pos[u] = -1;
     if (i < M) {
-      const int64_t t = ib[i];
+      const int64_t t = tv[u];
       if (t >= idx_lo && t < idx_hi && t - idx_lo < row_limit) {
         const uint32_t key = (uint32_t)(t - idx_lo);
         uint32_t h = hash_slot(key, log2ts);

@@ -44,10 +44,11 @@ __global__ void __launch_bounds__(128) plan_kernel(const float* __restrict__ g, 
   float lo = -60.0f, hi = 60.0f;
   for (int it = 0; it < iters; ++it) {
     const float mid = __fmul_rn(__fadd_rn(lo, hi), 0.5f);
-    float tot = 0.0f;
+    int cnt = 0;
 #pragma unroll
-    for (int i = 0; i < CPL; ++i) tot += fminf(fmaxf(rintf(__fmul_rn(__fsub_rn(lg[i], mid), 0.5f)), 0.0f), bm);
-    tot = warp_sum(tot);  // sum of small integers: exact in any order
+    for (int i = 0; i < CPL; ++i) cnt += (int)fminf(fmaxf(rintf(__fmul_rn(__fsub_rn(lg[i], mid), 0.5f)), 0.0f), bm);
+    // the depth sum is a small integer (<= 512): one warp reduction instruction, exact
+    const float tot = (float)__reduce_add_sync(0xffffffffu, cnt);
     if (tot > Br) lo = mid;
     else hi = mid;
   }

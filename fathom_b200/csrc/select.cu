@@ -240,7 +240,7 @@ __device__ void exact_select_row(const float* r, int64_t n, int64_t kk, int64_t 
 // Per level one pass counts the values still matching the prefix and histograms their next digit;
 // one warp then finds the digit.  It stops as soon as the prefix holds exactly `need` values.
 __device__ uint64_t refine_threshold(const uint64_t* s_v, int n, uint32_t top12, int64_t need, uint32_t* s_hist,
-                                     uint32_t* s_ctl) {
+                                     uint32_t* s_ctl, uint32_t* s_tmp) {
   uint64_t prefix = (uint64_t)top12 << 52;
   uint64_t pmask = 0xFFFull << 52;
   const int shifts[5] = {40, 28, 16, 4, 0};
@@ -266,17 +266,10 @@ __device__ uint64_t refine_threshold(const uint64_t* s_v, int n, uint32_t top12,
     if ((threadIdx.x & 31) == 0 && match) atomicAdd(&s_ctl[0], match);
     __syncthreads();
     if ((int64_t)s_ctl[0] == need) break;  // uniform: every value matching the prefix is taken
-    if (threadIdx.x < 32) {
-      uint32_t above;
-      const int b = warp_boundary_bin_smem(s_hist, need, &above);
-      if (threadIdx.x == 0) {
-        s_ctl[1] = (uint32_t)b;
-        s_ctl[2] = above;
-      }
-    }
-    __syncthreads();
-    need -= s_ctl[2];
-    prefix |= (uint64_t)s_ctl[1] << sh;
+    uint32_t above;
+    const int b = block_boundary_bin(s_hist, need, s_tmp, &above);
+    need -= above;
+    prefix |= (uint64_t)b << sh;
     pmask |= (uint64_t)(nb - 1) << sh;
     __syncthreads();  // s_ctl is rewritten by the next level
   }
@@ -352,6 +345,7 @@ __global__ void __launch_bounds__(FT) finalize_kernel(const float* __restrict__ 
   __shared__ uint32_t s_part[FT];
   __shared__ uint32_t s_warp[33];
   __shared__ uint32_t s_ctl[4];
+  __shared__ uint32_t s_tmp[66];
   __shared__ uint32_t s_cnt;
   __shared__ int s_res;
   const int64_t row = blockIdx.x;
@@ -375,7 +369,7 @@ __global__ void __launch_bounds__(FT) finalize_kernel(const float* __restrict__ 
     __syncthreads();
     const uint32_t tot = s_cnt;
     __syncthreads();
-    const uint64_t C = refine_threshold(s_buf, (int)cnt, top12, kk - (int64_t)tot, s_hist, s_ctl);
+    const uint64_t C = refine_threshold(s_buf, (int)cnt, top12, kk - (int64_t)tot, s_hist, s_ctl, s_tmp);
     if (threadIdx.x == 0) s_cnt = 0;
     __syncthreads();
     for (int i = threadIdx.x; i < (int)cnt; i += blockDim.x)
@@ -399,6 +393,7 @@ __global__ void __launch_bounds__(FT) merge_kernel(const float* __restrict__ cs,
   uint64_t* s_sel = s_dyn + CAP;
   __shared__ uint32_t s_hist[NBINS];
   __shared__ uint32_t s_ctl[4];
+  __shared__ uint32_t s_tmp[66];
   __shared__ uint32_t s_cnt;
   const int64_t row = blockIdx.x;
   for (int b = threadIdx.x; b < NBINS; b += blockDim.x) s_hist[b] = 0;
@@ -409,19 +404,10 @@ __global__ void __launch_bounds__(FT) merge_kernel(const float* __restrict__ cs,
     atomicAdd(&s_hist[v >> 52], 1u);
   }
   __syncthreads();
-  if (threadIdx.x < 32) {
-    uint32_t above;
-    const int b = warp_boundary_bin_smem(s_hist, kk, &above);
-    if (threadIdx.x == 0) {
-      s_ctl[1] = (uint32_t)b;
-      s_ctl[2] = above;
-    }
-  }
-  __syncthreads();
-  const uint32_t top12 = s_ctl[1];
-  const int64_t need = kk - (int64_t)s_ctl[2];
-  __syncthreads();
-  const uint64_t C = refine_threshold(s_buf, (int)m, top12, need, s_hist, s_ctl);
+  uint32_t above;
+  const uint32_t top12 = (uint32_t)block_boundary_bin(s_hist, kk, s_tmp, &above);
+  const int64_t need = kk - (int64_t)above;
+  const uint64_t C = refine_threshold(s_buf, (int)m, top12, need, s_hist, s_ctl, s_tmp);
   if (threadIdx.x == 0) s_cnt = 0;
   __syncthreads();
   for (int i = threadIdx.x; i < m; i += blockDim.x)
@@ -479,11 +465,14 @@ __global__ void __launch_bounds__(256) gmax_kernel(const float* __restrict__ sco
 constexpr int QT = 1024;   // threads of the group-selection CTA
 
 // One CTA per row.
-//   1 histogram of the top 12 key bits of the fully unmasked groups' keys (warp-aggregated shared
-//     atomics); tau = lower edge of the boundary bin, so at least kk unmasked tokens have key >= tau
+//   1 two-level histogram (top 12 key bits, then the next 12 bits inside the boundary bin) of the
+//     fully unmasked groups' keys (warp-aggregated shared atomics); tau = lower edge of the second
+//     level's boundary bin: at least kk groups, hence kk unmasked tokens, have a key >= tau, and tau
+//     lies within 2^-15 octave of the kk-th largest group key
 //   2 list the groups whose key reaches tau, read their scores, keep every token with key >= tau
 //     (masked tokens carry the key of -inf, as in the histogram path) as a candidate
-//   3 radix-refine the candidates to exactly kk, sort, write.
+//   3 at most 1024 candidates: one bitonic sort of all of them, the first kk win; more: radix-refine
+//     to exactly kk, then sort.
 // More than CAP listed groups or candidates (massive ties) takes the exact whole-row selection.
 __global__ void __launch_bounds__(QT) gsel_kernel(const float* __restrict__ scores, int64_t n, int64_t row_stride,
                                                   int64_t kk, int64_t mask_lo, int64_t mask_hi,
@@ -499,6 +488,7 @@ __global__ void __launch_bounds__(QT) gsel_kernel(const float* __restrict__ scor
   __shared__ uint32_t s_part[QT];
   __shared__ uint32_t s_warp[33];
   __shared__ uint32_t s_ctl[4];
+  __shared__ uint32_t s_tmp[66];
   __shared__ uint32_t s_cnt, s_nq;
   __shared__ int s_res;
   const int64_t row = blockIdx.x;
@@ -532,13 +522,32 @@ __global__ void __launch_bounds__(QT) gsel_kernel(const float* __restrict__ scor
     }
   }
   __syncthreads();
-  if (tid < 32) {
-    uint32_t above;
-    const int b = warp_boundary_bin_smem(s_hist, kk, &above);   // 0 when fewer than kk groups: all qualify
-    if (tid == 0) s_ctl[0] = (uint32_t)b;
+  uint32_t gabove;
+  const uint32_t b1 = (uint32_t)block_boundary_bin(s_hist, kk, s_tmp, &gabove);   // 0: all qualify
+  // second level: the next 12 bits of the group keys inside bin b1 (kk - gabove of them are needed)
+  for (int b = tid; b < NBINS; b += QT) s_hist[b] = 0;
+  __syncthreads();
+  for (int64_t base = 0; base < ng; base += (int64_t)QT * U) {
+    uint32_t bin[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int64_t g = base + (int64_t)u * QT + tid;
+      const uint32_t key = (g >= g_lo && g < g_hi) ? __ldg(gk + g) : 0u;
+      bin[u] = (g >= g_lo && g < g_hi && (key >> (32 - HBITS)) == b1) ? ((key >> (32 - 2 * HBITS)) & (NBINS - 1))
+                                                                      : (uint32_t)NBINS;
+    }
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      if (!__any_sync(0xffffffffu, bin[u] < (uint32_t)NBINS)) continue;
+      const uint32_t peers = __match_any_sync(0xffffffffu, bin[u]);
+      if (bin[u] < (uint32_t)NBINS && lane == __ffs(peers) - 1) atomicAdd(&s_hist[bin[u]], (uint32_t)__popc(peers));
+    }
   }
   __syncthreads();
-  const uint32_t tau = s_ctl[0] << (32 - HBITS);
+  uint32_t gabove2;
+  const uint32_t b2 = (uint32_t)block_boundary_bin(s_hist, kk - (int64_t)gabove, s_tmp, &gabove2);
+  // at least kk unmasked groups have a key >= tau (0 when fewer than kk groups: all qualify)
+  const uint32_t tau = (b1 << (32 - HBITS)) | (b2 << (32 - 2 * HBITS));
 
   // 2a: the groups whose key reaches tau, in a shared list
   for (int64_t base = 0; base < ng; base += (int64_t)QT * U) {
@@ -618,25 +627,30 @@ __global__ void __launch_bounds__(QT) gsel_kernel(const float* __restrict__ scor
   __syncthreads();
   const uint32_t cnt = s_cnt;
 
-  if (nq <= (uint32_t)CAP && cnt <= (uint32_t)CAP && cnt >= (uint32_t)kk) {
+  const bool fits = nq <= (uint32_t)CAP && cnt <= (uint32_t)CAP && cnt >= (uint32_t)kk;
+  if (fits && cnt <= (uint32_t)QT) {
+    // 3 (usual case): every candidate in one thread's register; one bitonic sort; the first kk win
+    uint64_t v = tid < (int)cnt ? s_buf[tid] : 0ull;
+    v = bitonic_desc_regs(v, next_pow2((int)cnt), s_sel);
+    int64_t* o = out_idx + row * out_stride;
+    if (tid < kk) {
+      o[tid] = (int64_t)(uint32_t)(~(uint32_t)v) + index_offset;
+      if (out_scores) out_scores[row * kk + tid] = key2f((uint32_t)(v >> 32));
+    }
+    for (int64_t i = tid; i < append_sink; i += QT) o[kk + i] = i;
+    for (int64_t i = tid; i < append_local; i += QT) o[kk + append_sink + i] = n - append_local + i;
+    return;
+  }
+  if (fits) {
     // 3: exactly kk of the candidates (at least kk of them exist, all distinct)
     for (int b = tid; b < NBINS; b += QT) s_hist[b] = 0;
     __syncthreads();
     for (int i = tid; i < (int)cnt; i += QT) atomicAdd(&s_hist[s_buf[i] >> 52], 1u);
     __syncthreads();
-    if (tid < 32) {
-      uint32_t above;
-      const int b = warp_boundary_bin_smem(s_hist, kk, &above);
-      if (tid == 0) {
-        s_ctl[1] = (uint32_t)b;
-        s_ctl[2] = above;
-      }
-    }
-    __syncthreads();
-    const uint32_t top12 = s_ctl[1];
-    const int64_t need = kk - (int64_t)s_ctl[2];
-    __syncthreads();
-    const uint64_t C = refine_threshold(s_buf, (int)cnt, top12, need, s_hist, s_ctl);
+    uint32_t above;
+    const uint32_t top12 = (uint32_t)block_boundary_bin(s_hist, kk, s_tmp, &above);
+    const int64_t need = kk - (int64_t)above;
+    const uint64_t C = refine_threshold(s_buf, (int)cnt, top12, need, s_hist, s_ctl, s_tmp);
     if (tid == 0) s_cnt = 0;
     __syncthreads();
     for (int i = tid; i < (int)cnt; i += QT)

@@ -36,7 +36,7 @@ constexpr size_t ws_bytes(int64_t rows) {
 // of the group's largest score), written by the scan's epilogue or by a pass over the scores.
 // If at least kk groups have a key >= tau, at least kk distinct tokens do, so the boundary bin of
 // the group keys bounds the kk-th largest token key from below; only the groups whose key reaches
-// it are read again.  Used when the fully unmasked groups number at least 2 * kk.
+// it are read again.  Used when the fully unmasked groups number at least 1.5 * kk.
 constexpr int GROUP = 32;
 constexpr int64_t n_groups(int64_t n) { return (n + GROUP - 1) / GROUP; }
 constexpr size_t gkey_bytes(int64_t rows, int64_t n) { return align256(rows * n_groups(n) * sizeof(uint32_t)); }
@@ -54,7 +54,7 @@ inline int64_t unmasked_groups(int64_t n, int64_t mask_lo, int64_t mask_hi) {
 }
 inline bool group_select_applies(int64_t rows, int64_t n, int64_t kk, int64_t mask_lo, int64_t mask_hi,
                                  size_t workspace_bytes) {
-  return unmasked_groups(n, mask_lo, mask_hi) >= 2 * kk && workspace_bytes >= gkey_bytes(rows, n);
+  return 2 * unmasked_groups(n, mask_lo, mask_hi) >= 3 * kk && workspace_bytes >= gkey_bytes(rows, n);
 }
 
 inline Workspace carve(void* base, int64_t rows) {
@@ -174,38 +174,61 @@ static __device__ int warp_boundary_bin(const uint32_t* hist, int64_t kk) {
   return m ? __shfl_sync(0xffffffffu, found, __ffs(m) - 1) : 0;
 }
 
-// The same search over a histogram in shared memory, also returning the count strictly above the bin.
-static __device__ int warp_boundary_bin_smem(const uint32_t* hist, int64_t kk, uint32_t* above_out) {
-  const int lane = threadIdx.x & 31;
-  constexpr int PER = NBINS / 32;
+// Boundary bin of a histogram in shared memory, found by the whole block (blockDim.x a multiple of 32
+// that divides NBINS by a multiple of 4, at most 1024): returns to every thread the largest bin b with
+// sum_{b' >= b} hist[b'] >= kk and the count strictly above b in *above_out; (0, 0) when the histogram
+// holds fewer than kk.  Each thread sums NBINS/blockDim consecutive bins (16-byte loads), a block-wide
+// suffix scan finds the one thread whose bins hold the crossing, which walks them.  s_tmp: 66 words.
+static __device__ int block_boundary_bin(const uint32_t* hist, int64_t kk, uint32_t* s_tmp, uint32_t* above_out) {
+  const int t = threadIdx.x, lane = t & 31, w = t >> 5, nw = blockDim.x >> 5;
+  const int per = NBINS / blockDim.x;
   uint32_t part = 0;
-  for (int i = 0; i < PER; ++i) part += hist[lane * PER + ((i + lane) & (PER - 1))];   // skewed: no bank conflicts
-  uint32_t suffix = part;
+  for (int i = 0; i < per; i += 4) {
+    const uint4 v = *reinterpret_cast<const uint4*>(hist + t * per + i);
+    part += v.x + v.y + v.z + v.w;
+  }
+  uint32_t suf = part;   // inclusive suffix sum over the lanes >= this one
 #pragma unroll
   for (int o = 1; o < 32; o <<= 1) {
-    const uint32_t y = __shfl_down_sync(0xffffffffu, suffix, o);
-    if (lane + o < 32) suffix += y;
+    const uint32_t y = __shfl_down_sync(0xffffffffu, suf, o);
+    if (lane + o < 32) suf += y;
   }
-  const uint32_t above = __shfl_down_sync(0xffffffffu, suffix, 1);
-  const uint32_t above_l = lane < 31 ? above : 0u;
-  int found = -1;
-  uint32_t found_above = 0;
-  if (suffix >= (uint32_t)kk && above_l < (uint32_t)kk) {
-    uint32_t run = above_l;
-    for (int b = PER - 1; b >= 0; --b) {
-      const uint32_t h = hist[lane * PER + b];
+  if (lane == 0) s_tmp[w] = suf;
+  __syncthreads();
+  if (w == 0) {
+    const uint32_t v = lane < nw ? s_tmp[lane] : 0u;
+    uint32_t s2 = v;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const uint32_t y = __shfl_down_sync(0xffffffffu, s2, o);
+      if (lane + o < 32) s2 += y;
+    }
+    s_tmp[32 + lane] = s2 - v;   // the warps above this one
+    if (lane == 0) {
+      s_tmp[64] = 0;
+      s_tmp[65] = 0;
+    }
+  }
+  __syncthreads();
+  const uint32_t incl = suf + s_tmp[32 + w];
+  const uint32_t above = incl - part;
+  if (incl >= (uint32_t)kk && above < (uint32_t)kk) {
+    uint32_t run = above;
+    for (int i = per - 1; i >= 0; --i) {
+      const uint32_t h = hist[t * per + i];
       if (run + h >= (uint32_t)kk) {
-        found = lane * PER + b;
-        found_above = run;
+        s_tmp[64] = (uint32_t)(t * per + i);
+        s_tmp[65] = run;
         break;
       }
       run += h;
     }
   }
-  const uint32_t m = __ballot_sync(0xffffffffu, found >= 0);
-  const int src = m ? __ffs(m) - 1 : 0;
-  *above_out = __shfl_sync(0xffffffffu, found_above, src);
-  return m ? __shfl_sync(0xffffffffu, found, src) : 0;
+  __syncthreads();
+  const int b = (int)s_tmp[64];
+  *above_out = s_tmp[65];
+  __syncthreads();   // s_tmp may be reused by the caller
+  return b;
 }
 
 // The whole selection over score rows: see select.cu.  With gkeys_ready the group keys are already in

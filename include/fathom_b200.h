@@ -115,7 +115,7 @@ size_t fathom_scan_select_workspace_bytes(int64_t BH, int G, int64_t n, int64_t 
  * top-kk of tokens in [mask_lo, mask_hi) plus index_offset to out_idx [r][out_stride] in (score desc,
  * index asc) order, followed by 0..append_sink-1 and n-append_local..n-1; the selected scores to
  * out_scores [r][kk] if not NULL.  sink_local_topk(k, sink, local) is kk = k-sink-local, mask
- * [sink, n-local), offset 0, append (sink, local), out_stride k.  When the row has at least 2*kk
+ * [sink, n-local), offset 0, append (sink, local), out_stride k.  When the row has at least 1.5*kk
  * fully unmasked 32-token groups, the scan also writes each group's largest score key to the
  * workspace and one selection kernel per row works from those (group-key path); otherwise the
  * histogram / collect / finalize passes run.  The workspace must hold the chosen path's buffers;
@@ -130,7 +130,7 @@ int fathom_scan_select(const float* q, int64_t BH, int G, int64_t n, int64_t sub
 /* ---------------------------------------------------------------- selection */
 
 /* Workspace bytes fathom_select_topk / fathom_sink_local_topk need for `rows` rows of n scores:
- * enough for either selection path (the group-key path, taken when a row has at least 2*kk fully
+ * enough for either selection path (the group-key path, taken when a row has at least 1.5*kk fully
  * unmasked 32-token groups and the workspace holds rows * ceil(n/32) keys; else the histogram path). */
 size_t fathom_select_workspace_bytes(int64_t rows, int64_t n, int64_t kk);
 
