@@ -295,6 +295,16 @@ def run_reference(a, rank, world):
 
 METRIC = "scanned key-rows/s and decode-step us at 1M ctx, 56-bit, k=512 (1/2/4/8 GPU)"
 
+# Per-launch traffic of the scan kernel relative to its algorithmic bytes, from one ncu capture each
+# (small cases of the same kernels; the ratio is size-independent because every launch reads each
+# needed plane run once):
+#   host run order, zero-copy: pcie__read_bytes.sum = 15,359,488 B for 14,151,680 algorithmic bytes
+#     (T = 262144, 8 KV heads, budget 48, bulk-copy instance)
+#   HBM order: dram__bytes_read.sum + dram__bytes_write.sum = 8,893,952 + 0 B for 7,069,127 algorithmic
+#     bytes (T = 131072, 8 KV heads, budget 48, 16-byte cp.async instance)
+TRAFFIC_RATIO_HOST = 15359488 / 14151680
+TRAFFIC_RATIO_HBM = 8893952 / 7069127
+
 
 def config_dict(a, world):
     return {"workload": "config2: host-resident index + K/V rows, Qwen3-8B attention shape, decode step",
@@ -388,7 +398,10 @@ def hbm_figure(a, dev, bp, off, peaks, spec="config1"):
             "value": rows / (ms * 1e-3), "unit": "key-rows/s", "ms_per_step": ms,
             "scan_ms_per_layer": scan_ms, "scan_timing": f"{nl} scan launches in one CUDA graph, mean per launch",
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
-                         "frac": achieved / peaks["hbm_gbs"], "traffic": None,
+                         "frac": achieved / peaks["hbm_gbs"],
+                         "traffic": float(np.mean(byts)) * TRAFFIC_RATIO_HBM if spec == "config1" else None,
+                         "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum per launch (same shape)"
+                                           if spec == "config1" else "not captured",
                          "bytes_per_launch": float(np.mean(byts))},
             "bits_per_row": float(np.mean(byts)) * 8 / (n * BH)}
 
@@ -496,7 +509,8 @@ def main():
             "data": "synthetic (seeded lognormal-channel keys/values/queries)", "config": config_dict(a, world),
             "bits_per_row": bits_row,
             "roofline": {"bound": "host_link", "achieved": achieved, "peak": link, "unit": "GB/s",
-                         "frac": achieved / link, "traffic": None,
+                         "frac": achieved / link, "traffic": float(np.mean(byts)) * TRAFFIC_RATIO_HOST,
+                         "traffic_source": "ncu pcie__read_bytes.sum per launch, T=262144 capture scaled by units",
                          "bytes_per_launch": float(np.mean(byts)),
                          "kernel": "scan (zero-copy reads of the host index)",
                          "peak_source": "pinned H2D cudaMemcpy of 1 GiB measured in this run"},
