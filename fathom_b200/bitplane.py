@@ -111,12 +111,13 @@ _BUDGETS = {}
 
 def _budget_tensor(value, BH, dev):
     """A [BH] fp32 tensor holding a scalar budget, kept per (device, BH, value) so a decode loop does not
-    launch a fill kernel per call; made fresh while a CUDA graph is being captured (the graph then owns it)."""
-    if torch.cuda.is_current_stream_capturing():
-        return torch.full((BH,), value, device=dev)
+    launch a fill kernel per call.  A tensor first needed while a CUDA graph is being captured is made
+    fresh for that graph (which then owns it) and not kept."""
     key = (dev.index if dev.index is not None else torch.cuda.current_device(), BH, value)
     t = _BUDGETS.get(key)
     if t is None:
+        if torch.cuda.is_current_stream_capturing():
+            return torch.full((BH,), value, device=dev)
         if len(_BUDGETS) > 256:
             _BUDGETS.clear()
         t = _BUDGETS[key] = torch.full((BH,), value, device=dev)

@@ -2,7 +2,8 @@
 // (scripts/B_e2e_offload_v2.py:73-83 gather_rows, :226-244 offload_attn tail;
 //  HBM twin scripts/B_kernel_bench.py:26-31 gather_attn).
 //
-// decode attention, three launches:
+// decode attention from host-resident rows, three launches (device-resident rows: one launch of
+// attend_direct_kernel, which reads each pick's rows in place):
 //   1 dedupe   one CTA per (batch, kv-head): the G*k picks go into a shared-memory hash table,
 //              a block scan ranks the distinct indices; slot map (query head, pick) -> unique row,
 //              the unique index list (in table order) and its length.
@@ -28,6 +29,16 @@ constexpr int AU = 4;         // picks per warp iteration
 constexpr int MAX_M = 16384;  // G*k per (batch, kv-head) handled by one dedupe CTA
 
 size_t align256(size_t x) { return (x + 255) & ~(size_t)255; }
+
+// True for device (HBM) memory; false for host memory (mapped or not), managed memory and unknown pointers.
+bool device_memory(const void* p) {
+  cudaPointerAttributes a;
+  if (cudaPointerGetAttributes(&a, p) != cudaSuccess) {
+    cudaGetLastError();   // clear the error of an unregistered pointer
+    return false;
+  }
+  return a.type == cudaMemoryTypeDevice;
+}
 
 struct DecodeWs {
   int32_t* slot;       // [BH][M] pick -> unique row (-1: not owned)
@@ -305,6 +316,114 @@ __global__ void __launch_bounds__(AW * 32) attend_kernel(const float* __restrict
   }
 }
 
+// Device-resident rows (HBM): no dedupe and no staging.  Same CTA layout and math as attend_kernel,
+// but each pick's K and V rows are read from their source by index (repeats of a row across the
+// query heads of a KV head are L2 hits).  A pick outside [idx_lo, idx_hi) or beyond the readable rows
+// (n_host rows of the source, then recent_cap rows of the recent buffer) is skipped.
+__global__ void __launch_bounds__(AW * 32) attend_direct_kernel(const float* __restrict__ q, int G, int64_t k,
+                                                                const int64_t* __restrict__ idx, int64_t idx_lo,
+                                                                int64_t idx_hi, const uint16_t* __restrict__ ksrc,
+                                                                const uint16_t* __restrict__ vsrc, int64_t cap,
+                                                                int64_t row_stride, int64_t n_host,
+                                                                const uint16_t* __restrict__ krec,
+                                                                const uint16_t* __restrict__ vrec, int64_t recent_cap,
+                                                                float* __restrict__ out_f32,
+                                                                uint16_t* __restrict__ out_bf16,
+                                                                float* __restrict__ out_packed) {
+  __shared__ float s_m[AW], s_l[AW];
+  __shared__ float s_acc[AW][D];
+  const int64_t bhg = blockIdx.x;
+  const int64_t bh = bhg / G;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const float4 qv = *reinterpret_cast<const float4*>(q + bhg * D + lane * 4);
+  const int64_t* ib = idx + bhg * k;
+  const float scale = rsqrtf((float)D);
+  float m = -INFINITY, l = 0.0f, a0 = 0.0f, a1 = 0.0f, a2 = 0.0f, a3 = 0.0f;
+  for (int64_t r0 = (int64_t)warp * AU; r0 < k; r0 += (int64_t)AW * AU) {
+    bool ok[AU];
+    uint2 kw[AU], vw[AU];
+#pragma unroll
+    for (int u = 0; u < AU; ++u) {
+      const int64_t t = r0 + u < k ? ib[r0 + u] : -1;
+      ok[u] = r0 + u < k && t >= idx_lo && t < idx_hi && t - idx_lo < n_host + recent_cap;
+      kw[u] = make_uint2(0, 0);
+      vw[u] = make_uint2(0, 0);
+      if (ok[u]) {
+        const int64_t rel = t - idx_lo;
+        const uint16_t* kr = rel < n_host ? ksrc + (bh * cap + rel) * row_stride : krec + (bh * recent_cap + rel - n_host) * D;
+        const uint16_t* vr = rel < n_host ? vsrc + (bh * cap + rel) * row_stride : vrec + (bh * recent_cap + rel - n_host) * D;
+        kw[u] = *reinterpret_cast<const uint2*>(kr + lane * 4);
+        vw[u] = *reinterpret_cast<const uint2*>(vr + lane * 4);
+      }
+    }
+    float sc[AU];
+#pragma unroll
+    for (int u = 0; u < AU; ++u)
+      sc[u] = qv.x * bf16lo(kw[u].x) + qv.y * bf16hi(kw[u].x) + qv.z * bf16lo(kw[u].y) + qv.w * bf16hi(kw[u].y);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+#pragma unroll
+      for (int u = 0; u < AU; ++u) sc[u] += __shfl_xor_sync(0xffffffffu, sc[u], o);
+    }
+    float mx = m;
+#pragma unroll
+    for (int u = 0; u < AU; ++u) {
+      sc[u] = ok[u] ? sc[u] * scale : -INFINITY;
+      mx = fmaxf(mx, sc[u]);
+    }
+    if (mx == -INFINITY) continue;  // nothing owned yet
+    const float corr = m == -INFINITY ? 0.0f : expf(m - mx);
+    l *= corr;
+    a0 *= corr;
+    a1 *= corr;
+    a2 *= corr;
+    a3 *= corr;
+#pragma unroll
+    for (int u = 0; u < AU; ++u) {
+      const float p = sc[u] == -INFINITY ? 0.0f : expf(sc[u] - mx);
+      l += p;
+      a0 = fmaf(p, bf16lo(vw[u].x), a0);
+      a1 = fmaf(p, bf16hi(vw[u].x), a1);
+      a2 = fmaf(p, bf16lo(vw[u].y), a2);
+      a3 = fmaf(p, bf16hi(vw[u].y), a3);
+    }
+    m = mx;
+  }
+  if (lane == 0) {
+    s_m[warp] = m;
+    s_l[warp] = l;
+  }
+  s_acc[warp][lane * 4 + 0] = a0;
+  s_acc[warp][lane * 4 + 1] = a1;
+  s_acc[warp][lane * 4 + 2] = a2;
+  s_acc[warp][lane * 4 + 3] = a3;
+  __syncthreads();
+  if (tid < D) {
+    float Mx = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < AW; ++w) Mx = fmaxf(Mx, s_m[w]);
+    float L = 0.0f, O = 0.0f;
+#pragma unroll
+    for (int w = 0; w < AW; ++w) {
+      const float e = s_m[w] == -INFINITY ? 0.0f : expf(s_m[w] - Mx);
+      L = fmaf(s_l[w], e, L);
+      O = fmaf(s_acc[w][tid], e, O);
+    }
+    if (out_packed) {
+      float* pk = out_packed + bhg * (D + 2);
+      pk[tid] = O;
+      if (tid == 0) {
+        pk[D] = Mx;
+        pk[D + 1] = L;
+      }
+    } else {
+      const float o = O / L;
+      if (out_f32) out_f32[bhg * D + tid] = o;
+      if (out_bf16) out_bf16[bhg * D + tid] = __bfloat16_as_ushort(__float2bfloat16_rn(o));
+    }
+  }
+}
+
 // out = sum_p o_p e^(m_p - M) / sum_p l_p e^(m_p - M), M = max_p m_p: log-sum-exp merge of the
 // partial attention of P context shards.  One CTA of 128 threads per (batch, query head).
 __global__ void __launch_bounds__(D) combine_kernel(const float* __restrict__ parts, int64_t P, int64_t rows,
@@ -359,12 +478,20 @@ int run_decode(const float* q, int64_t BH, int G, const int64_t* idx, int64_t k,
   FATHOM_REQUIRE((reinterpret_cast<uintptr_t>(K_src) & 15) == 0 && (reinterpret_cast<uintptr_t>(V_src) & 15) == 0 &&
                      (reinterpret_cast<uintptr_t>(q) & 15) == 0,
                  FATHOM_ERR_SHAPE, "decode_attention: q and the K/V sources must be 16-byte aligned");
-  DecodeWs w = carve(workspace, BH, M);
   FATHOM_REQUIRE(cap < 0xFFFFFFFFLL && n_host + recent_cap < 0xFFFFFFFFLL, FATHOM_ERR_UNSUPPORTED,
                  "decode_attention: row indices must fit 32 bits");
   if (kv_row_stride == 0) kv_row_stride = D;
   FATHOM_REQUIRE(kv_row_stride >= D && kv_row_stride % 8 == 0, FATHOM_ERR_SHAPE,
                  "decode_attention: kv_row_stride must be >= 128 and a multiple of 8 elements");
+  if (device_memory(K_src) && device_memory(V_src) &&
+      (recent_cap == 0 || (device_memory(K_recent) && device_memory(V_recent)))) {
+    // rows already in HBM: each pick's rows are read in place (one launch; the workspace is unused)
+    attend_direct_kernel<<<(unsigned)(BH * G), AW * 32, 0, st>>>(q, G, k, idx, idx_lo, idx_hi, K_src, V_src, cap,
+                                                                 kv_row_stride, n_host, K_recent, V_recent, recent_cap,
+                                                                 out_f32, out_bf16, out_packed);
+    return check_launch("decode_attention");
+  }
+  DecodeWs w = carve(workspace, BH, M);
   int log2ts = 10;
   while ((1 << log2ts) < 2 * M) ++log2ts;           // load factor <= 1/2
   FATHOM_REQUIRE((1 << log2ts) <= MAX_TS, FATHOM_ERR_UNSUPPORTED, "decode_attention: too many picks");
