@@ -97,8 +97,10 @@ __device__ uint32_t block_exclusive_scan(uint32_t v, uint32_t* s_warp, uint32_t*
 }
 
 constexpr uint32_t EMPTY = 0xFFFFFFFFu;
-constexpr int MAX_TS = 32768;         // hash table slots (128 KB of shared memory)
+constexpr int MAX_TS = 32768;         // hash table slots (128 KB of shared memory; + M keys, 2 x NB bins)
 constexpr int PICKS_PER_THREAD = MAX_M / DT;
+constexpr int NB = 2048;              // rank buckets (high bits of the row index)
+constexpr int MAX_PER = MAX_TS / DT;  // table slots per dedupe thread
 
 __device__ __forceinline__ uint32_t hash_slot(uint32_t key, int log2ts) {
   return (key * 0x9E3779B1u) >> (32 - log2ts);
@@ -106,17 +108,24 @@ __device__ __forceinline__ uint32_t hash_slot(uint32_t key, int log2ts) {
 
 // One CTA per (batch, kv-head).  Every owned pick is inserted into an open-addressing table in
 // shared memory (atomicCAS, linear probing; the table has at least twice as many slots as picks,
-// so a probe sequence always ends at an empty slot or at its own key).  A block scan over the
-// table then ranks the distinct indices; each pick remembers its table slot and reads its rank.
+// so a probe sequence always ends at an empty slot or at its own key).  The distinct indices are
+// then ranked in ascending order: a counting pass over NB buckets of their high bits, a block scan,
+// a scatter into bucket order, and within each (small) bucket a count of the smaller keys.  The
+// unique list is therefore sorted, so the gather walks the source in address order (fewer address
+// translations per byte over the host link), and every rank is independent of the insert order.
+// Each pick remembers its table slot and reads its rank.
 __global__ void __launch_bounds__(DT) dedupe_kernel(const int64_t* __restrict__ idx, int64_t M, int64_t idx_lo,
-                                                    int64_t idx_hi, int64_t row_limit, int log2ts,
+                                                    int64_t idx_hi, int64_t row_limit, int log2ts, int bshift,
                                                     int32_t* __restrict__ slot,
                                                     int64_t* __restrict__ uniq, int32_t* __restrict__ ucount) {
-  extern __shared__ uint32_t s_tab[];  // 1 << log2ts slots
+  extern __shared__ uint32_t s_tab[];  // 1 << log2ts slots, then M keys in bucket order
   __shared__ uint32_t s_warp[33];
+  __shared__ uint32_t s_bin[NB], s_cur[NB];
   const int64_t bh = blockIdx.x;
   const int TS = 1 << log2ts;
+  uint32_t* s_sorted = s_tab + TS;
   for (int i = threadIdx.x; i < TS; i += blockDim.x) s_tab[i] = EMPTY;
+  for (int b = threadIdx.x; b < NB; b += blockDim.x) s_bin[b] = 0u;
   __syncthreads();
   const int64_t* ib = idx + bh * M;
   int pos[PICKS_PER_THREAD];
@@ -147,21 +156,39 @@ __global__ void __launch_bounds__(DT) dedupe_kernel(const int64_t* __restrict__ 
     }
   }
   __syncthreads();
-  // rank the occupied slots (each thread a contiguous chunk of the table)
+  // ascending ranks of the distinct keys (each thread a contiguous chunk of the table)
   const int per = TS / DT > 0 ? TS / DT : 1;
   const int h0 = threadIdx.x * per;
-  uint32_t cnt = 0;
-  for (int h = h0; h < h0 + per && h < TS; ++h) cnt += s_tab[h] != EMPTY;
+  const int h1 = h0 + per < TS ? h0 + per : TS;
+  for (int h = h0; h < h1; ++h)
+    if (s_tab[h] != EMPTY) atomicAdd(&s_bin[s_tab[h] >> bshift], 1u);
+  __syncthreads();
+  uint32_t bsum = 0;   // bins 2t, 2t+1 of thread t (NB = 2 * DT)
+  const uint32_t c0 = s_bin[2 * threadIdx.x], c1 = s_bin[2 * threadIdx.x + 1];
   uint32_t total;
-  uint32_t r = block_exclusive_scan(cnt, s_warp, &total);
+  bsum = block_exclusive_scan(c0 + c1, s_warp, &total);
+  s_bin[2 * threadIdx.x] = bsum;
+  s_bin[2 * threadIdx.x + 1] = bsum + c0;
+  s_cur[2 * threadIdx.x] = bsum;
+  s_cur[2 * threadIdx.x + 1] = bsum + c0;
+  __syncthreads();
+  for (int h = h0; h < h1; ++h)
+    if (s_tab[h] != EMPTY) s_sorted[atomicAdd(&s_cur[s_tab[h] >> bshift], 1u)] = s_tab[h];
+  __syncthreads();   // s_cur[b] is now the end of bucket b
+  uint32_t myrank[MAX_PER];
   int64_t* ul = uniq + bh * M;
-  for (int h = h0; h < h0 + per && h < TS; ++h) {
-    const uint32_t key = s_tab[h];
-    if (key != EMPTY) {
-      ul[r] = (int64_t)key;
-      s_tab[h] = r++;     // the slot now holds the rank (keys are no longer needed)
-    }
+  for (int h = h0; h < h1; ++h) {
+    const uint32_t x = s_tab[h];
+    if (x == EMPTY) continue;
+    const uint32_t b = x >> bshift;
+    uint32_t r = s_bin[b];
+    for (uint32_t t = s_bin[b]; t < s_cur[b]; ++t) r += s_sorted[t] < x;
+    myrank[h - h0] = r;
+    ul[r] = (int64_t)x;
   }
+  __syncthreads();   // every key read: the slots may now hold ranks
+  for (int h = h0; h < h1; ++h)
+    if (s_tab[h] != EMPTY) s_tab[h] = myrank[h - h0];
   __syncthreads();
   int32_t* sl = slot + bh * M;
 #pragma unroll
@@ -495,11 +522,13 @@ int run_decode(const float* q, int64_t BH, int G, const int64_t* idx, int64_t k,
   int log2ts = 10;
   while ((1 << log2ts) < 2 * M) ++log2ts;           // load factor <= 1/2
   FATHOM_REQUIRE((1 << log2ts) <= MAX_TS, FATHOM_ERR_UNSUPPORTED, "decode_attention: too many picks");
-  const size_t smem = (size_t)sizeof(uint32_t) << log2ts;
+  const size_t smem = sizeof(uint32_t) * (((size_t)1 << log2ts) + (size_t)M);   // table + keys in bucket order
   cudaFuncSetAttribute(dedupe_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  int bshift = 0;   // NB buckets cover the readable rows [0, n_host + recent_cap)
+  while (((n_host + recent_cap - 1) >> bshift) >= NB) ++bshift;
   // picks at or beyond the readable rows (n_host host rows + recent_cap device rows) are ignored
-  dedupe_kernel<<<(unsigned)BH, DT, smem, st>>>(idx, M, idx_lo, idx_hi, n_host + recent_cap, log2ts, w.slot, w.uniq,
-                                                w.ucount);
+  dedupe_kernel<<<(unsigned)BH, DT, smem, st>>>(idx, M, idx_lo, idx_hi, n_host + recent_cap, log2ts, bshift, w.slot,
+                                                w.uniq, w.ucount);
   dim3 ggrid((unsigned)cdiv(M, GROWS), (unsigned)BH);
   gather_kernel<<<ggrid, GT, 0, st>>>(w.ucount, w.uniq, M, reinterpret_cast<const uint4*>(K_src),
                                       reinterpret_cast<const uint4*>(V_src), cap, kv_row_stride / 8, n_host,
