@@ -471,8 +471,9 @@ constexpr int QT = 1024;   // threads of the group-selection CTA
 //     lies within 2^-15 octave of the kk-th largest group key
 //   2 list the groups whose key reaches tau, read their scores, keep every token with key >= tau
 //     (masked tokens carry the key of -inf, as in the histogram path) as a candidate
-//   3 at most 1024 candidates: one bitonic sort of all of them, the first kk win; more: radix-refine
-//     to exactly kk, then sort.
+//   3 at most 4096 candidates: a counting rank (bins of the key above tau, then a count of the larger
+//     values in the candidate's bin); ranks below kk are written in place.  More: radix-refine to
+//     exactly kk, then sort.
 // More than CAP listed groups or candidates (massive ties) takes the exact whole-row selection.
 __global__ void __launch_bounds__(QT) gsel_kernel(const float* __restrict__ scores, int64_t n, int64_t row_stride,
                                                   int64_t kk, int64_t mask_lo, int64_t mask_hi,
@@ -628,14 +629,59 @@ __global__ void __launch_bounds__(QT) gsel_kernel(const float* __restrict__ scor
   const uint32_t cnt = s_cnt;
 
   const bool fits = nq <= (uint32_t)CAP && cnt <= (uint32_t)CAP && cnt >= (uint32_t)kk;
-  if (fits && cnt <= (uint32_t)QT) {
-    // 3 (usual case): every candidate in one thread's register; one bitonic sort; the first kk win
-    uint64_t v = tid < (int)cnt ? s_buf[tid] : 0ull;
-    v = bitonic_desc_regs(v, next_pow2((int)cnt), s_sel);
+  if (fits && cnt <= (uint32_t)MAX_KK) {
+    // 3 (usual case): a counting rank.  Candidates go to NBINS bins of (key - tau) >> bshift, highest bin
+    // first; a descending scan of the bin counts gives each bin's first rank, and a candidate's rank is
+    // that plus the number of larger values in its bin (bins hold a few candidates).  Ranks < kk are
+    // written straight to their output positions.
+    uint32_t kmax = 0;
+    for (int i = tid; i < (int)cnt; i += QT) kmax = max(kmax, (uint32_t)(s_buf[i] >> 32));
+    kmax = __reduce_max_sync(0xffffffffu, kmax);
+    if (lane == 0) s_tmp[tid >> 5] = kmax;
+    for (int b = tid; b < NBINS; b += QT) s_hist[b] = 0;
+    __syncthreads();
+    kmax = s_tmp[lane];   // 32 warps
+    kmax = __reduce_max_sync(0xffffffffu, kmax);
+    int bshift = 0;
+    while (((kmax - tau) >> bshift) >= (uint32_t)NBINS) ++bshift;
+    for (int i = tid; i < (int)cnt; i += QT)
+      atomicAdd(&s_hist[(NBINS - 1) - (((uint32_t)(s_buf[i] >> 32) - tau) >> bshift)], 1u);   // descending bins
+    __syncthreads();
+    uint32_t* s_cur = reinterpret_cast<uint32_t*>(s_buf + MAX_KK);   // bin cursors (the unused half of s_buf)
+    {
+      const int per = NBINS / QT;   // 4 bins per thread
+      uint32_t c[NBINS / QT], tot = 0;
+#pragma unroll
+      for (int u = 0; u < per; ++u) {
+        c[u] = s_hist[tid * per + u];
+        tot += c[u];
+      }
+      uint32_t all;
+      uint32_t start = block_exclusive_scan(tot, s_warp, &all);
+#pragma unroll
+      for (int u = 0; u < per; ++u) {
+        s_hist[tid * per + u] = start;   // first rank of the bin
+        s_cur[tid * per + u] = start;
+        start += c[u];
+      }
+    }
+    __syncthreads();
+    for (int i = tid; i < (int)cnt; i += QT) {
+      const uint64_t v = s_buf[i];
+      const uint32_t b = (NBINS - 1) - (((uint32_t)(v >> 32) - tau) >> bshift);
+      s_sel[atomicAdd(&s_cur[b], 1u)] = v;
+    }
+    __syncthreads();   // s_cur[b] is now the end of bin b
     int64_t* o = out_idx + row * out_stride;
-    if (tid < kk) {
-      o[tid] = (int64_t)(uint32_t)(~(uint32_t)v) + index_offset;
-      if (out_scores) out_scores[row * kk + tid] = key2f((uint32_t)(v >> 32));
+    for (int i = tid; i < (int)cnt; i += QT) {
+      const uint64_t v = s_buf[i];
+      const uint32_t b = (NBINS - 1) - (((uint32_t)(v >> 32) - tau) >> bshift);
+      uint32_t r = s_hist[b];
+      for (uint32_t t = s_hist[b]; t < s_cur[b]; ++t) r += s_sel[t] > v;
+      if (r < (uint32_t)kk) {
+        o[r] = (int64_t)(uint32_t)(~(uint32_t)v) + index_offset;
+        if (out_scores) out_scores[row * kk + r] = key2f((uint32_t)(v >> 32));
+      }
     }
     for (int64_t i = tid; i < append_sink; i += QT) o[kk + i] = i;
     for (int64_t i = tid; i < append_local; i += QT) o[kk + append_sink + i] = n - append_local + i;
