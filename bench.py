@@ -348,31 +348,43 @@ def hbm_figure(a, dev, bp, off, peaks, spec="config1"):
     k_tot = sp["k"] + a.sink + a.local
     scores = torch.empty(BH, G, n, device=dev)
 
-    def step():
+    def step(budget):
         for L, lay in enumerate(layers):
-            plan = bp.make_plan(lay.g, a.budget)
+            plan = bp.make_plan(lay.g, budget)
             idx = bp.scan_topk(lay.store, lay.q, plan, k_tot, a.sink, a.local, scores=scores)
             off.decode_attention(lay.q, idx, kvs[L][0], kvs[L][1], n)
 
-    for _ in range(a.warmup):
-        step()
-    torch.cuda.synchronize()
-    # graph of the whole step removes the per-launch host cost from the per-layer latency
-    g = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(g):
-        step()
-    torch.cuda.synchronize()
-    for _ in range(a.warmup):
-        g.replay()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    torch.cuda.profiler.start()
-    e0.record()
-    for _ in range(a.steps):
-        g.replay()
-    e1.record()
-    torch.cuda.synchronize()
-    torch.cuda.profiler.stop()
-    ms = e0.elapsed_time(e1) / a.steps
+    def timed_step(budget, profile=False):
+        for _ in range(a.warmup):
+            step(budget)
+        torch.cuda.synchronize()
+        # graph of the whole step removes the per-launch host cost from the per-layer latency
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            step(budget)
+        torch.cuda.synchronize()
+        for _ in range(a.warmup):
+            g.replay()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        if profile:
+            torch.cuda.profiler.start()
+        e0.record()
+        for _ in range(a.steps):
+            g.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        if profile:
+            torch.cuda.profiler.stop()
+        del g
+        return e0.elapsed_time(e1) / a.steps
+
+    ms = timed_step(a.budget, profile=True)
+    sweep = []
+    if spec == "config1":
+        # the other budgets of the configuration (about 47 and 92 bits per row on real keys)
+        for b in (40.0, 80.0):
+            bits = float(np.mean([bp.bytes_planes(bp.make_plan(lay.g, b)["t"], n) for lay in layers])) * 8 / (n * BH)
+            sweep.append({"budget": b, "bits_per_row": bits, "ms_per_step": timed_step(b)})
     # the scan kernel alone, back to back in a graph (launch gaps removed): mean duration per layer
     plans = [bp.make_plan(lay.g, a.budget) for lay in layers]
     gs = torch.cuda.CUDAGraph()
@@ -392,7 +404,7 @@ def hbm_figure(a, dev, bp, off, peaks, spec="config1"):
     byts = [lay.bytes for lay in layers]
     achieved = float(np.mean(byts)) / (scan_ms * 1e-3) / 1e9
     rows = n * BH * nl
-    del g, gs, layers, kvs
+    del gs, layers, kvs
     torch.cuda.empty_cache()
     return {"workload": sp["workload"],
             "value": rows / (ms * 1e-3), "unit": "key-rows/s", "ms_per_step": ms,
@@ -403,7 +415,8 @@ def hbm_figure(a, dev, bp, off, peaks, spec="config1"):
                          "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum per launch (same shape)"
                                            if spec == "config1" else "not captured",
                          "bytes_per_launch": float(np.mean(byts))},
-            "bits_per_row": float(np.mean(byts)) * 8 / (n * BH)}
+            "bits_per_row": float(np.mean(byts)) * 8 / (n * BH),
+            **({"budget_sweep": sweep} if sweep else {})}
 
 
 # ------------------------------------------------------------------ main

@@ -186,7 +186,10 @@ size_t fathom_decode_workspace_bytes(int64_t BH, int G, int64_t k);
 /* Decode attention over selected rows (offload_attn tail, scripts/B_e2e_offload_v2.py:226-244;
  * HBM twin gather_attn, scripts/B_kernel_bench.py:26-31):
  *   q [BH][G][128] fp32; idx [BH][G][k] int64 token indices.
- *   Each unique index of a KV head is fetched once.  Index < n_host reads row idx of
+ *   Rows in host memory (mapped aliases): each unique index of a KV head is fetched once over the
+ *   link, in ascending order, into the workspace.  Rows in device memory (K_src, V_src and the recent
+ *   buffers all device allocations): each pick's rows are read in place and the workspace is unused.
+ *   Either way the sums run in pick order, so both give the same bits.  Index < n_host reads row idx of
  *   K_src/V_src [BH][cap] rows of 128 bf16, kv_row_stride elements apart (0 = 128; 256 for a cache
  *   that interleaves each token's K and V rows), in device memory or a mapped host alias; index >= n_host
  *   reads row idx-n_host of K_recent/V_recent [BH][recent_cap][128] bf16 (device).
