@@ -25,7 +25,6 @@ constexpr int DT = 1024;      // dedupe threads
 constexpr int GT = 256;       // gather threads
 constexpr int GROWS = 64;     // unique rows per gather CTA
 constexpr int AW = 32;        // attend warps
-constexpr int AU = 4;         // picks per warp iteration
 constexpr int MAX_M = 16384;  // G*k per (batch, kv-head) handled by one dedupe CTA
 
 size_t align256(size_t x) { return (x + 255) & ~(size_t)255; }
@@ -248,49 +247,29 @@ __global__ void __launch_bounds__(GT) gather_kernel(const int32_t* __restrict__ 
 __device__ __forceinline__ float bf16lo(uint32_t w) { return __uint_as_float(w << 16); }
 __device__ __forceinline__ float bf16hi(uint32_t w) { return __uint_as_float(w & 0xffff0000u); }
 
-// out_packed != NULL: partial form, [BH*G][130] = (sum_r e^(s_r - m) V_r, m, l).
-__global__ void __launch_bounds__(AW * 32) attend_kernel(const float* __restrict__ q, int G, int64_t k, int64_t M,
-                                                         const int32_t* __restrict__ slot,
-                                                         const uint16_t* __restrict__ kstage,
-                                                         const uint16_t* __restrict__ vstage,
-                                                         float* __restrict__ out_f32, uint16_t* __restrict__ out_bf16,
-                                                         float* __restrict__ out_packed) {
-  __shared__ float s_m[AW], s_l[AW];
-  __shared__ float s_acc[AW][D];
-  const int64_t bhg = blockIdx.x;
-  const int64_t bh = bhg / G, g = bhg % G;
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const float4 qv = *reinterpret_cast<const float4*>(q + bhg * D + lane * 4);
-  const int32_t* sl = slot + bh * M + g * k;
-  const uint16_t* kb = kstage + bh * M * D + lane * 4;
-  const uint16_t* vb = vstage + bh * M * D + lane * 4;
-  const float scale = rsqrtf((float)D);
+// Picks of a warp, DU at a time, with the online softmax (shared by attend_kernel and
+// attend_direct_kernel so both sum in the same order and give the same bits).  row_of(u) returns
+// the K and V row pointers of the warp's chunk pick s0+u (nullptr: not owned).
+struct WarpSoftmax {
   float m = -INFINITY, l = 0.0f, a0 = 0.0f, a1 = 0.0f, a2 = 0.0f, a3 = 0.0f;
-  for (int64_t r0 = (int64_t)warp * AU; r0 < k; r0 += (int64_t)AW * AU) {
-    int32_t sr[AU];
-    uint2 kw[AU], vw[AU];
+  __device__ __forceinline__ void add(const float4& qv, const bool (&ok)[8], const uint2 (&kw)[8],
+                                      const uint2 (&vw)[8], float scale) {
+    float sc[8];
 #pragma unroll
-    for (int u = 0; u < AU; ++u) {
-      sr[u] = r0 + u < k ? sl[r0 + u] : -1;
-      kw[u] = sr[u] >= 0 ? *reinterpret_cast<const uint2*>(kb + (int64_t)sr[u] * D) : make_uint2(0, 0);
-      vw[u] = sr[u] >= 0 ? *reinterpret_cast<const uint2*>(vb + (int64_t)sr[u] * D) : make_uint2(0, 0);
-    }
-    float sc[AU];
-#pragma unroll
-    for (int u = 0; u < AU; ++u)
+    for (int u = 0; u < 8; ++u)
       sc[u] = qv.x * bf16lo(kw[u].x) + qv.y * bf16hi(kw[u].x) + qv.z * bf16lo(kw[u].y) + qv.w * bf16hi(kw[u].y);
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) {
 #pragma unroll
-      for (int u = 0; u < AU; ++u) sc[u] += __shfl_xor_sync(0xffffffffu, sc[u], o);
+      for (int u = 0; u < 8; ++u) sc[u] += __shfl_xor_sync(0xffffffffu, sc[u], o);
     }
     float mx = m;
 #pragma unroll
-    for (int u = 0; u < AU; ++u) {
-      sc[u] = sr[u] >= 0 ? sc[u] * scale : -INFINITY;
+    for (int u = 0; u < 8; ++u) {
+      sc[u] = ok[u] ? sc[u] * scale : -INFINITY;
       mx = fmaxf(mx, sc[u]);
     }
-    if (mx == -INFINITY) continue;  // nothing owned yet
+    if (mx == -INFINITY) return;  // nothing owned yet
     const float corr = m == -INFINITY ? 0.0f : expf(m - mx);
     l *= corr;
     a0 *= corr;
@@ -298,24 +277,32 @@ __global__ void __launch_bounds__(AW * 32) attend_kernel(const float* __restrict
     a2 *= corr;
     a3 *= corr;
 #pragma unroll
-    for (int u = 0; u < AU; ++u) {
-      const float p = sc[u] == -INFINITY ? 0.0f : expf(sc[u] - mx);
-      l += p;
-      a0 = fmaf(p, bf16lo(vw[u].x), a0);
-      a1 = fmaf(p, bf16hi(vw[u].x), a1);
-      a2 = fmaf(p, bf16lo(vw[u].y), a2);
-      a3 = fmaf(p, bf16hi(vw[u].y), a3);
+    for (int u = 0; u < 8; ++u) {
+      const float pr = sc[u] == -INFINITY ? 0.0f : expf(sc[u] - mx);
+      l += pr;
+      a0 = fmaf(pr, bf16lo(vw[u].x), a0);
+      a1 = fmaf(pr, bf16hi(vw[u].x), a1);
+      a2 = fmaf(pr, bf16lo(vw[u].y), a2);
+      a3 = fmaf(pr, bf16hi(vw[u].y), a3);
     }
     m = mx;
   }
+};
+constexpr int DU = 8;   // rows in flight per warp
+
+// Merges the AW warp states of a CTA and writes the (batch, query head) output or partial.
+__device__ __forceinline__ void attend_finish(const WarpSoftmax& ws, int64_t bhg, float* s_m, float* s_l,
+                                              float (*s_acc)[D], float* __restrict__ out_f32,
+                                              uint16_t* __restrict__ out_bf16, float* __restrict__ out_packed) {
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   if (lane == 0) {
-    s_m[warp] = m;
-    s_l[warp] = l;
+    s_m[warp] = ws.m;
+    s_l[warp] = ws.l;
   }
-  s_acc[warp][lane * 4 + 0] = a0;
-  s_acc[warp][lane * 4 + 1] = a1;
-  s_acc[warp][lane * 4 + 2] = a2;
-  s_acc[warp][lane * 4 + 3] = a3;
+  s_acc[warp][lane * 4 + 0] = ws.a0;
+  s_acc[warp][lane * 4 + 1] = ws.a1;
+  s_acc[warp][lane * 4 + 2] = ws.a2;
+  s_acc[warp][lane * 4 + 3] = ws.a3;
   __syncthreads();
   if (tid < D) {
     float Mx = -INFINITY;
@@ -343,10 +330,54 @@ __global__ void __launch_bounds__(AW * 32) attend_kernel(const float* __restrict
   }
 }
 
-// Device-resident rows (HBM): no dedupe and no staging.  Same CTA layout and math as attend_kernel,
-// but each pick's K and V rows are read from their source by index (repeats of a row across the
-// query heads of a KV head are L2 hits).  A pick outside [idx_lo, idx_hi) or beyond the readable rows
-// (n_host rows of the source, then recent_cap rows of the recent buffer) is skipped.
+// Host-resident rows, after dedupe + gather: one CTA of AW warps per (batch, query head); warp w owns
+// picks [w*PW, w*PW + PW), PW = ceil(k / AW).  Per 32 picks the warp loads their staging slots with
+// one coalesced load, then reads the staged K and V rows DU picks at a time (8 bytes per lane of each
+// 256-byte row).  out_packed != NULL: partial form, [BH*G][130] = (sum_r e^(s_r - m) V_r, m, l).
+__global__ void __launch_bounds__(AW * 32) attend_kernel(const float* __restrict__ q, int G, int64_t k, int64_t M,
+                                                         const int32_t* __restrict__ slot,
+                                                         const uint16_t* __restrict__ kstage,
+                                                         const uint16_t* __restrict__ vstage,
+                                                         float* __restrict__ out_f32, uint16_t* __restrict__ out_bf16,
+                                                         float* __restrict__ out_packed) {
+  __shared__ float s_m[AW], s_l[AW];
+  __shared__ float s_acc[AW][D];
+  const int64_t bhg = blockIdx.x;
+  const int64_t bh = bhg / G, g = bhg % G;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const float4 qv = *reinterpret_cast<const float4*>(q + bhg * D + lane * 4);
+  const int32_t* sl = slot + bh * M + g * k;
+  const uint16_t* kb = kstage + bh * M * D + lane * 4;
+  const uint16_t* vb = vstage + bh * M * D + lane * 4;
+  const float scale = rsqrtf((float)D);
+  const int64_t PW = (k + AW - 1) / AW;
+  const int64_t p0 = (int64_t)warp * PW;
+  const int64_t p1 = p0 + PW < k ? p0 + PW : k;
+  WarpSoftmax ws;
+  for (int64_t c0 = p0; c0 < p1; c0 += 32) {   // uniform per warp
+    const int32_t mine = c0 + lane < p1 ? sl[c0 + lane] : -1;
+    const int nc = (int)(p1 - c0 < 32 ? p1 - c0 : 32);
+    for (int s0 = 0; s0 < nc; s0 += DU) {
+      bool ok[DU];
+      uint2 kw[DU], vw[DU];
+#pragma unroll
+      for (int u = 0; u < DU; ++u) {
+        int32_t r = __shfl_sync(0xffffffffu, mine, (s0 + u) & 31);
+        if (s0 + u >= nc) r = -1;
+        ok[u] = r >= 0;
+        kw[u] = ok[u] ? *reinterpret_cast<const uint2*>(kb + (int64_t)r * D) : make_uint2(0, 0);
+        vw[u] = ok[u] ? *reinterpret_cast<const uint2*>(vb + (int64_t)r * D) : make_uint2(0, 0);
+      }
+      ws.add(qv, ok, kw, vw, scale);
+    }
+  }
+  attend_finish(ws, bhg, s_m, s_l, s_acc, out_f32, out_bf16, out_packed);
+}
+
+// Device-resident rows (HBM): no dedupe and no staging.  The layout and summation order of
+// attend_kernel, with each pick's K and V rows read in place by index (rows repeated across the
+// query heads of a KV head are L2 hits).  A pick outside [idx_lo, idx_hi) or beyond the readable
+// rows (n_host rows of the source, then recent_cap rows of the recent buffer) is skipped.
 __global__ void __launch_bounds__(AW * 32) attend_direct_kernel(const float* __restrict__ q, int G, int64_t k,
                                                                 const int64_t* __restrict__ idx, int64_t idx_lo,
                                                                 int64_t idx_hi, const uint16_t* __restrict__ ksrc,
@@ -361,94 +392,44 @@ __global__ void __launch_bounds__(AW * 32) attend_direct_kernel(const float* __r
   __shared__ float s_acc[AW][D];
   const int64_t bhg = blockIdx.x;
   const int64_t bh = bhg / G;
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const float4 qv = *reinterpret_cast<const float4*>(q + bhg * D + lane * 4);
   const int64_t* ib = idx + bhg * k;
   const float scale = rsqrtf((float)D);
-  float m = -INFINITY, l = 0.0f, a0 = 0.0f, a1 = 0.0f, a2 = 0.0f, a3 = 0.0f;
-  for (int64_t r0 = (int64_t)warp * AU; r0 < k; r0 += (int64_t)AW * AU) {
-    bool ok[AU];
-    uint2 kw[AU], vw[AU];
+  const int64_t PW = (k + AW - 1) / AW;
+  const int64_t p0 = (int64_t)warp * PW;
+  const int64_t p1 = p0 + PW < k ? p0 + PW : k;
+  WarpSoftmax ws;
+  for (int64_t c0 = p0; c0 < p1; c0 += 32) {   // uniform per warp
+    // this lane's pick of the chunk: its row (< 2^32 - 1, checked by the launcher), or -1 when not owned
+    int32_t rel = -1;
+    if (c0 + lane < p1) {
+      const int64_t t = ib[c0 + lane];
+      if (t >= idx_lo && t < idx_hi && t - idx_lo < n_host + recent_cap) rel = (int32_t)(uint32_t)(t - idx_lo);
+    }
+    const int nc = (int)(p1 - c0 < 32 ? p1 - c0 : 32);
+    for (int s0 = 0; s0 < nc; s0 += DU) {
+      bool ok[DU];
+      uint2 kw[DU], vw[DU];
 #pragma unroll
-    for (int u = 0; u < AU; ++u) {
-      const int64_t t = r0 + u < k ? ib[r0 + u] : -1;
-      ok[u] = r0 + u < k && t >= idx_lo && t < idx_hi && t - idx_lo < n_host + recent_cap;
-      kw[u] = make_uint2(0, 0);
-      vw[u] = make_uint2(0, 0);
-      if (ok[u]) {
-        const int64_t rel = t - idx_lo;
-        const uint16_t* kr = rel < n_host ? ksrc + (bh * cap + rel) * row_stride : krec + (bh * recent_cap + rel - n_host) * D;
-        const uint16_t* vr = rel < n_host ? vsrc + (bh * cap + rel) * row_stride : vrec + (bh * recent_cap + rel - n_host) * D;
-        kw[u] = *reinterpret_cast<const uint2*>(kr + lane * 4);
-        vw[u] = *reinterpret_cast<const uint2*>(vr + lane * 4);
+      for (int u = 0; u < DU; ++u) {
+        int32_t rr = __shfl_sync(0xffffffffu, rel, (s0 + u) & 31);
+        if (s0 + u >= nc) rr = -1;
+        ok[u] = rr != -1;
+        kw[u] = make_uint2(0, 0);
+        vw[u] = make_uint2(0, 0);
+        if (ok[u]) {
+          const int64_t r = (int64_t)(uint32_t)rr;
+          const uint16_t* kr = r < n_host ? ksrc + (bh * cap + r) * row_stride : krec + (bh * recent_cap + r - n_host) * D;
+          const uint16_t* vr = r < n_host ? vsrc + (bh * cap + r) * row_stride : vrec + (bh * recent_cap + r - n_host) * D;
+          kw[u] = *reinterpret_cast<const uint2*>(kr + lane * 4);
+          vw[u] = *reinterpret_cast<const uint2*>(vr + lane * 4);
+        }
       }
-    }
-    float sc[AU];
-#pragma unroll
-    for (int u = 0; u < AU; ++u)
-      sc[u] = qv.x * bf16lo(kw[u].x) + qv.y * bf16hi(kw[u].x) + qv.z * bf16lo(kw[u].y) + qv.w * bf16hi(kw[u].y);
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-#pragma unroll
-      for (int u = 0; u < AU; ++u) sc[u] += __shfl_xor_sync(0xffffffffu, sc[u], o);
-    }
-    float mx = m;
-#pragma unroll
-    for (int u = 0; u < AU; ++u) {
-      sc[u] = ok[u] ? sc[u] * scale : -INFINITY;
-      mx = fmaxf(mx, sc[u]);
-    }
-    if (mx == -INFINITY) continue;  // nothing owned yet
-    const float corr = m == -INFINITY ? 0.0f : expf(m - mx);
-    l *= corr;
-    a0 *= corr;
-    a1 *= corr;
-    a2 *= corr;
-    a3 *= corr;
-#pragma unroll
-    for (int u = 0; u < AU; ++u) {
-      const float p = sc[u] == -INFINITY ? 0.0f : expf(sc[u] - mx);
-      l += p;
-      a0 = fmaf(p, bf16lo(vw[u].x), a0);
-      a1 = fmaf(p, bf16hi(vw[u].x), a1);
-      a2 = fmaf(p, bf16lo(vw[u].y), a2);
-      a3 = fmaf(p, bf16hi(vw[u].y), a3);
-    }
-    m = mx;
-  }
-  if (lane == 0) {
-    s_m[warp] = m;
-    s_l[warp] = l;
-  }
-  s_acc[warp][lane * 4 + 0] = a0;
-  s_acc[warp][lane * 4 + 1] = a1;
-  s_acc[warp][lane * 4 + 2] = a2;
-  s_acc[warp][lane * 4 + 3] = a3;
-  __syncthreads();
-  if (tid < D) {
-    float Mx = -INFINITY;
-#pragma unroll
-    for (int w = 0; w < AW; ++w) Mx = fmaxf(Mx, s_m[w]);
-    float L = 0.0f, O = 0.0f;
-#pragma unroll
-    for (int w = 0; w < AW; ++w) {
-      const float e = s_m[w] == -INFINITY ? 0.0f : expf(s_m[w] - Mx);
-      L = fmaf(s_l[w], e, L);
-      O = fmaf(s_acc[w][tid], e, O);
-    }
-    if (out_packed) {
-      float* pk = out_packed + bhg * (D + 2);
-      pk[tid] = O;
-      if (tid == 0) {
-        pk[D] = Mx;
-        pk[D + 1] = L;
-      }
-    } else {
-      const float o = O / L;
-      if (out_f32) out_f32[bhg * D + tid] = o;
-      if (out_bf16) out_bf16[bhg * D + tid] = __bfloat16_as_ushort(__float2bfloat16_rn(o));
+      ws.add(qv, ok, kw, vw, scale);
     }
   }
+  attend_finish(ws, bhg, s_m, s_l, s_acc, out_f32, out_bf16, out_packed);
 }
 
 // out = sum_p o_p e^(m_p - M) / sum_p l_p e^(m_p - M), M = max_p m_p: log-sum-exp merge of the
