@@ -4,7 +4,14 @@
 // Output order is (score descending, index ascending); every tie is broken by the index, so
 // the selection is deterministic and a context-sharded scan merges to the same list.
 //
-// Three launches on the caller's stream:
+// Two paths, chosen per call (select_common.cuh: group_select_applies):
+//
+// Group-key path (a row has at least 1.5 kk fully unmasked 32-token groups): the scan's epilogue (or
+// gmax_kernel over existing scores) writes the key of each group's largest score, then gsel_kernel,
+// one CTA per row, bounds the threshold from those keys, reads only the groups that reach it and
+// ranks the candidates (see gsel_kernel).
+//
+// Histogram path (dense k), three launches on the caller's stream:
 //   1 hist      many CTAs per row: 4096-bin histogram of the top 12 bits of the order-
 //               preserving key of every unmasked score (masked tokens get the key of -inf);
 //               shared-memory histogram, flushed to the row's global histogram with atomics.
