@@ -3,7 +3,7 @@
 //  HBM twin scripts/B_kernel_bench.py:26-31 gather_attn).
 //
 // decode attention from host-resident rows, three launches (device-resident rows: one launch of
-// attend_direct_kernel, which reads each pick's rows in place):
+// attend_direct_kernel or attend_direct_cluster_kernel, which read each pick's rows in place):
 //   1 dedupe   one CTA per (batch, kv-head): the G*k picks go into a shared-memory hash table,
 //              a block scan ranks the distinct indices; slot map (query head, pick) -> unique row,
 //              the unique index list (in table order) and its length.
@@ -18,6 +18,8 @@
 // the partial form writes the unnormalised output with its (max, sum of exp).
 #include "common.cuh"
 
+#include <cooperative_groups.h>
+
 namespace fathom {
 namespace {
 
@@ -28,6 +30,18 @@ constexpr int AW = 32;        // attend warps
 constexpr int MAX_M = 16384;  // G*k per (batch, kv-head) handled by one dedupe CTA
 
 size_t align256(size_t x) { return (x + 255) & ~(size_t)255; }
+
+int sm_count() {
+  static int cached[64] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+  if (cached[dev] == 0) {
+    int v = 0;
+    cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev);
+    cached[dev] = v > 0 ? v : 148;
+  }
+  return cached[dev];
+}
 
 // True for device (HBM) memory; false for host memory (mapped or not), managed memory and unknown pointers.
 bool device_memory(const void* p) {
@@ -247,9 +261,8 @@ __global__ void __launch_bounds__(GT) gather_kernel(const int32_t* __restrict__ 
 __device__ __forceinline__ float bf16lo(uint32_t w) { return __uint_as_float(w << 16); }
 __device__ __forceinline__ float bf16hi(uint32_t w) { return __uint_as_float(w & 0xffff0000u); }
 
-// Picks of a warp, DU at a time, with the online softmax (shared by attend_kernel and
-// attend_direct_kernel so both sum in the same order and give the same bits).  row_of(u) returns
-// the K and V row pointers of the warp's chunk pick s0+u (nullptr: not owned).
+// The online softmax of one warp over its picks, DU at a time (shared by attend_kernel and the two
+// in-place kernels, so all three sum in the same order and give the same bits).
 struct WarpSoftmax {
   float m = -INFINITY, l = 0.0f, a0 = 0.0f, a1 = 0.0f, a2 = 0.0f, a3 = 0.0f;
   __device__ __forceinline__ void add(const float4& qv, const bool (&ok)[8], const uint2 (&kw)[8],
@@ -374,8 +387,8 @@ __global__ void __launch_bounds__(AW * 32) attend_kernel(const float* __restrict
   attend_finish(ws, bhg, s_m, s_l, s_acc, out_f32, out_bf16, out_packed);
 }
 
-// Device-resident rows (HBM): no dedupe and no staging.  The layout and summation order of
-// attend_kernel, with each pick's K and V rows read in place by index (rows repeated across the
+// Device-resident rows (HBM), many query heads: no dedupe and no staging.  The layout and summation
+// order of attend_kernel, with each pick's K and V rows read in place by index (rows repeated across the
 // query heads of a KV head are L2 hits).  A pick outside [idx_lo, idx_hi) or beyond the readable
 // rows (n_host rows of the source, then recent_cap rows of the recent buffer) is skipped.
 __global__ void __launch_bounds__(AW * 32) attend_direct_kernel(const float* __restrict__ q, int G, int64_t k,
@@ -430,6 +443,105 @@ __global__ void __launch_bounds__(AW * 32) attend_direct_kernel(const float* __r
     }
   }
   attend_finish(ws, bhg, s_m, s_l, s_acc, out_f32, out_bf16, out_packed);
+}
+
+// Device-resident rows (HBM), few query heads (fewer than SMs): the pick layout and summation order
+// of attend_kernel, spread over a cluster of CS CTAs of AW / CS warps each: global warp w (CTA w / 8,
+// warp w % 8) owns picks [w*PW, w*PW + PW), PW = ceil(k / AW), and reads each pick's K and V rows in
+// place by index (rows repeated across the query heads of a KV head are L2 hits).  The cluster's
+// first CTA merges the AW warp states through distributed shared memory in global warp order, so the
+// result has the bits of attend_kernel.  A pick outside [idx_lo, idx_hi) or beyond the readable rows
+// (n_host rows of the source, then recent_cap rows of the recent buffer) is skipped.
+constexpr int CS = 4;            // CTAs per (batch, query head)
+constexpr int CW = AW / CS;      // warps per CTA
+__global__ void __launch_bounds__(CW * 32, 1) attend_direct_cluster_kernel(const float* __restrict__ q, int G, int64_t k,
+                                                                const int64_t* __restrict__ idx, int64_t idx_lo,
+                                                                int64_t idx_hi, const uint16_t* __restrict__ ksrc,
+                                                                const uint16_t* __restrict__ vsrc, int64_t cap,
+                                                                int64_t row_stride, int64_t n_host,
+                                                                const uint16_t* __restrict__ krec,
+                                                                const uint16_t* __restrict__ vrec, int64_t recent_cap,
+                                                                float* __restrict__ out_f32,
+                                                                uint16_t* __restrict__ out_bf16,
+                                                                float* __restrict__ out_packed) {
+  namespace cg = cooperative_groups;
+  cg::cluster_group cluster = cg::this_cluster();
+  __shared__ float s_m[CW], s_l[CW];
+  __shared__ float s_acc[CW][D];
+  const unsigned crank = cluster.block_rank();
+  const int64_t bhg = blockIdx.x / CS;
+  const int64_t bh = bhg / G;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int gw = (int)crank * CW + warp;   // global warp of the (batch, query head)
+  const float4 qv = *reinterpret_cast<const float4*>(q + bhg * D + lane * 4);
+  const int64_t* ib = idx + bhg * k;
+  const float scale = rsqrtf((float)D);
+  const int64_t PW = (k + AW - 1) / AW;
+  const int64_t p0 = (int64_t)gw * PW;
+  const int64_t p1 = p0 + PW < k ? p0 + PW : k;
+  WarpSoftmax ws;
+  for (int64_t c0 = p0; c0 < p1; c0 += 32) {   // uniform per warp
+    // this lane's pick of the chunk: its row (< 2^32 - 1, checked by the launcher), or -1 when not owned
+    int32_t rel = -1;
+    if (c0 + lane < p1) {
+      const int64_t t = ib[c0 + lane];
+      if (t >= idx_lo && t < idx_hi && t - idx_lo < n_host + recent_cap) rel = (int32_t)(uint32_t)(t - idx_lo);
+    }
+    const int nc = (int)(p1 - c0 < 32 ? p1 - c0 : 32);
+    for (int s0 = 0; s0 < nc; s0 += DU) {
+      bool ok[DU];
+      uint2 kw[DU], vw[DU];
+#pragma unroll
+      for (int u = 0; u < DU; ++u) {
+        int32_t rr = __shfl_sync(0xffffffffu, rel, (s0 + u) & 31);
+        if (s0 + u >= nc) rr = -1;
+        ok[u] = rr != -1;
+        kw[u] = make_uint2(0, 0);
+        vw[u] = make_uint2(0, 0);
+        if (ok[u]) {
+          const int64_t r = (int64_t)(uint32_t)rr;
+          const uint16_t* kr = r < n_host ? ksrc + (bh * cap + r) * row_stride : krec + (bh * recent_cap + r - n_host) * D;
+          const uint16_t* vr = r < n_host ? vsrc + (bh * cap + r) * row_stride : vrec + (bh * recent_cap + r - n_host) * D;
+          kw[u] = *reinterpret_cast<const uint2*>(kr + lane * 4);
+          vw[u] = *reinterpret_cast<const uint2*>(vr + lane * 4);
+        }
+      }
+      ws.add(qv, ok, kw, vw, scale);
+    }
+  }
+  if (lane == 0) {
+    s_m[warp] = ws.m;
+    s_l[warp] = ws.l;
+  }
+  s_acc[warp][lane * 4 + 0] = ws.a0;
+  s_acc[warp][lane * 4 + 1] = ws.a1;
+  s_acc[warp][lane * 4 + 2] = ws.a2;
+  s_acc[warp][lane * 4 + 3] = ws.a3;
+  cluster.sync();   // every CTA's warp states are written
+  if (crank == 0 && tid < D) {
+    float Mx = -INFINITY;
+    for (int w = 0; w < AW; ++w) Mx = fmaxf(Mx, *cluster.map_shared_rank(&s_m[w % CW], w / CW));
+    float L = 0.0f, O = 0.0f;
+    for (int w = 0; w < AW; ++w) {
+      const float mw = *cluster.map_shared_rank(&s_m[w % CW], w / CW);
+      const float e = mw == -INFINITY ? 0.0f : expf(mw - Mx);
+      L = fmaf(*cluster.map_shared_rank(&s_l[w % CW], w / CW), e, L);
+      O = fmaf(*cluster.map_shared_rank(&s_acc[w % CW][tid], w / CW), e, O);
+    }
+    if (out_packed) {
+      float* pk = out_packed + bhg * (D + 2);
+      pk[tid] = O;
+      if (tid == 0) {
+        pk[D] = Mx;
+        pk[D + 1] = L;
+      }
+    } else {
+      const float o = O / L;
+      if (out_f32) out_f32[bhg * D + tid] = o;
+      if (out_bf16) out_bf16[bhg * D + tid] = __bfloat16_as_ushort(__float2bfloat16_rn(o));
+    }
+  }
+  cluster.sync();   // the first CTA has read the others' shared memory
 }
 
 // out = sum_p o_p e^(m_p - M) / sum_p l_p e^(m_p - M), M = max_p m_p: log-sum-exp merge of the
@@ -494,9 +606,28 @@ int run_decode(const float* q, int64_t BH, int G, const int64_t* idx, int64_t k,
   if (device_memory(K_src) && device_memory(V_src) &&
       (recent_cap == 0 || (device_memory(K_recent) && device_memory(V_recent)))) {
     // rows already in HBM: each pick's rows are read in place (one launch; the workspace is unused)
-    attend_direct_kernel<<<(unsigned)(BH * G), AW * 32, 0, st>>>(q, G, k, idx, idx_lo, idx_hi, K_src, V_src, cap,
-                                                                 kv_row_stride, n_host, K_recent, V_recent, recent_cap,
-                                                                 out_f32, out_bf16, out_packed);
+    if (BH * G >= (int64_t)sm_count()) {   // enough CTAs of 32 warps to fill the GPU
+      attend_direct_kernel<<<(unsigned)(BH * G), AW * 32, 0, st>>>(q, G, k, idx, idx_lo, idx_hi, K_src, V_src, cap,
+                                                                   kv_row_stride, n_host, K_recent, V_recent,
+                                                                   recent_cap, out_f32, out_bf16, out_packed);
+      return check_launch("decode_attention");
+    }
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)(BH * G * CS));
+    cfg.blockDim = dim3(CW * 32);
+    cfg.dynamicSmemBytes = 0;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = CS;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, attend_direct_cluster_kernel, q, G, k, idx, idx_lo, idx_hi, K_src, V_src,
+                                             cap, kv_row_stride, n_host, K_recent, V_recent, recent_cap, out_f32,
+                                             out_bf16, out_packed);
+    if (e != cudaSuccess) return set_error(FATHOM_ERR_CUDA, "decode_attention: launch: %s", cudaGetErrorString(e));
     return check_launch("decode_attention");
   }
   DecodeWs w = carve(workspace, BH, M);
