@@ -120,6 +120,49 @@ def bytes_planes(t, n):
     return float(((t.sum(-1) * 8 + (t > 0).sum(-1) * 2) * nblocks(n)).sum())
 
 
+# ---------------------------------------------------------------- Chan4 comparator store
+def pack_chan4(code, sub=SUB_HBM):
+    """kernels/bitplane.py:67-74.  Codes uint8 [..., n, D] -> channel-major 4-bit store int32
+    [..., nsb, D, sub, 8]: nibble k of word m of block s = code of token 64*(sb*sub+s) + 8*m + k
+    (zero padded to whole superblocks; two's complement in int32)."""
+    code = np.asarray(code, np.uint8)
+    *lead, n, d = code.shape
+    nb = nblocks(n)
+    nsb = (nb + sub - 1) // sub
+    cb = np.zeros((*lead, nsb * sub * BLK, d), np.int64)
+    cb[..., :n, :] = code
+    cb = cb.reshape(*lead, nsb, sub, 8, 8, d)
+    k = np.arange(8, dtype=np.int64).reshape(8, 1)
+    words = (cb << (4 * k)).sum(-2)                                    # [..., nsb, sub, 8, d]
+    words = words.astype(np.uint32).view(np.int32)
+    nl = len(lead)
+    return np.ascontiguousarray(np.transpose(words, (*range(nl), nl, nl + 3, nl + 1, nl + 2)))
+
+
+def bytes_chan4(nact, n):
+    """kernels/bitplane.py:79-80.  Bytes one chan4 scan moves: sum_bh nact * (32 + 2) * nblk."""
+    return float((np.asarray(nact, np.float64) * (32 + 2) * nblocks(n)).sum())
+
+
+def channel_list(active):
+    """kernels/bitplane.py:128-132.  active bool [BH, D] -> act int32 [BH, D] (active channels ascending,
+    then the inactive ones ascending) and nact int32 [BH]."""
+    active = np.asarray(active, bool)
+    order = np.argsort((~active).astype(np.int8), axis=-1, kind="stable")
+    return order.astype(np.int32), active.sum(-1).astype(np.int32)
+
+
+def scan_chan4(q, code, scales, active):
+    """kernels/bitplane.py:365-370 (scan_chan4_reference): the full 4-bit dequantised keys of the active
+    channels, (c - 7.5) * s / 8, against q [BH, G, D] -> fp32 [BH, G, n]."""
+    q = np.asarray(q, np.float32)
+    out = np.empty((q.shape[0], q.shape[1], code.shape[-2]), np.float32)
+    for b in range(q.shape[0]):
+        val = dequant_planes(code[b], scales[b], np.full(code.shape[-1], 4)) * np.asarray(active[b], np.float32)[None]
+        out[b] = q[b] @ val.T
+    return out
+
+
 # ---------------------------------------------------------------- plan
 def _log2_f32(g):
     """log2 in float32 of max(g, 1e-30), rounded from a double-precision log2."""

@@ -1,6 +1,7 @@
 """The CPU oracle against the reference's own outputs (golden fixtures) and the paper's
 worked example.  CPU only."""
 import hashlib
+import os
 
 import numpy as np
 import pytest
@@ -118,3 +119,32 @@ def test_merge_candidates_is_global_topk():
         cs.append(np.take_along_axis(scores, ch[local], -1))
     merged = O.merge_candidates(np.concatenate(cs, -1), np.concatenate(ci, -1), 100)
     assert np.array_equal(merged, full)
+
+
+CHAN4_CASES = ("c1", "c2", "c3", "c4")
+
+
+@pytest.mark.parametrize("c", CHAN4_CASES)
+def test_chan4_oracle_matches_reference(c):
+    """pack_chan4, channel_list, bytes_chan4 and the chan4 scan against the reference's own outputs
+    (scan_chan4_reference and, for power-of-two G, its Triton scan_chan4_kernel)."""
+    z = np.load(os.path.join(os.path.dirname(__file__), "golden", "chan4.npz"))
+    K = O.bf16_to_f32(z[f"{c}_K_bf16"].view(np.uint16))
+    sub = int(z[f"{c}_sub"])
+    code, sc = O.quantise_u4(K)
+    assert np.array_equal(code, z[f"{c}_code"])
+    assert np.array_equal(O.pack_chan4(code, sub), z[f"{c}_chan_k"])
+    planes_k, scales_k = O.to_superblocks(O.pack_planes(code), sc, sub)
+    assert np.array_equal(scales_k.view(np.int16), z[f"{c}_scales_k"])
+    act, nact = O.channel_list(z[f"{c}_active"])
+    assert np.array_equal(act, z[f"{c}_act"]) and np.array_equal(nact, z[f"{c}_nact"])
+    assert O.bytes_chan4(nact, K.shape[1]) == float(z[f"{c}_bytes"])
+    s = O.scan_chan4(z[f"{c}_q"], code, sc, z[f"{c}_active"])
+    for key in (f"{c}_scores", f"{c}_scores_triton"):
+        if key not in z.files:
+            continue
+        ref = z[key]
+        # c3's fp16 amax overflow makes whole rows +-inf in the reference too: same positions and signs
+        assert np.array_equal(np.isinf(s), np.isinf(ref)) and np.array_equal(s[np.isinf(s)], ref[np.isinf(ref)])
+        fin = np.isfinite(ref).all(-1)
+        assert score_rel_err(s[fin], ref[fin]) < 1e-5
