@@ -241,6 +241,92 @@ class PlaneStore:
 
 
 # ------------------------------------------------------------------ selection
+# ------------------------------------------------------------------ Chan4 comparator store
+def pack_chan4(code):
+    """codes uint8 [BH, n, D] -> channel-major 4-bit store int32 [BH, nsb, D, SUB, 8]: nibble k of word m
+    of a block is the code of token 8m+k of that block (kernels/bitplane.py:67-74; module SUB)."""
+    require_cuda(code)
+    BH, n, d = code.shape
+    if d != D:
+        raise ValueError(f"pack_chan4: codes must be [BH, n, {D}]")
+    nsb = math.ceil(_nblk(n) / SUB)
+    out = torch.empty(BH, nsb, D, SUB, 8, dtype=torch.int32, device=code.device)
+    check(lib().fathom_pack_chan4(ptr(code.contiguous().to(torch.uint8)), BH, n, SUB, ptr(out), stream_of(code.device)),
+          "pack_chan4")
+    return out
+
+
+def channel_list(active):
+    """active bool [BH, D] -> act int32 [BH, D] (active channels ascending, then the inactive ones
+    ascending), nact int32 [BH] (kernels/bitplane.py:128-132)."""
+    require_cuda(active)
+    BH, d = active.shape
+    if d != D:
+        raise ValueError(f"channel_list: active must be [BH, {D}]")
+    a = active.contiguous().to(torch.uint8)
+    act = torch.empty(BH, D, dtype=torch.int32, device=active.device)
+    nact = torch.empty(BH, dtype=torch.int32, device=active.device)
+    check(lib().fathom_channel_list(ptr(a), BH, ptr(act), ptr(nact), stream_of(active.device)), "channel_list")
+    return act, nact
+
+
+def bytes_chan4(nact, n):
+    """Bytes a Chan4Store.scan moves: sum_bh nact * (32 + 2) per 64-token block (kernels/bitplane.py:79-80)."""
+    return float((nact.float() * (32 + 2) * _nblk(n)).sum())
+
+
+class Chan4Store:
+    """The reference's comparator store (kernels/bitplane.py:342-355): K [BH, n, D] quantised as for
+    PlaneStore, kept channel-major at full 4 bits (chan_k [BH, nsb, D, SUB, 8] int32) with the same
+    block scales (scales_k [BH, nsb, D, SUB] fp16); scan(q, act, nact) reads the first nact[bh]
+    channels of act at 4 bits.  Attributes as the reference: BH, n, code, scales_blk, chan_k,
+    scales_k, nsb; the class attribute cfg is accepted and ignored (one CUDA scan serves all)."""
+    cfg = {"NB": 2, "KK": 1, "num_warps": 1, "num_stages": 1}
+
+    def __init__(self, K, scale_dtype=torch.float16):
+        require_cuda(K)
+        self.BH, self.n, d = K.shape
+        assert d == D
+        if K.dtype not in _lib.DTYPE_CODE:
+            K = K.float()
+        if scale_dtype not in (torch.float16, torch.float32):
+            raise TypeError("Chan4Store: scale_dtype must be torch.float16 or torch.float32")
+        self.sub = SUB
+        nb = _nblk(self.n)
+        self.nsb = math.ceil(nb / self.sub)
+        dev = K.device
+        Kc = K if K.stride(-1) == 1 and K.stride(-2) == D else K.contiguous()
+        self.code = torch.empty(self.BH, self.n, D, dtype=torch.uint8, device=dev)
+        self.scales_blk = torch.empty(self.BH, nb, D, dtype=scale_dtype, device=dev)
+        self.scales_k = torch.empty(self.BH, self.nsb, D, self.sub, dtype=torch.float16, device=dev)
+        planes = torch.empty(self.BH, self.nsb, D, 4, self.sub, dtype=torch.int64, device=dev)   # construction only
+        check(lib().fathom_quantise_pack(ptr(Kc), _lib.DTYPE_CODE[Kc.dtype], self.BH, self.n, Kc.stride(0), self.sub,
+                                         int(scale_dtype == torch.float16), ptr(self.code), ptr(self.scales_blk),
+                                         int(scale_dtype == torch.float32), ptr(planes), ptr(self.scales_k),
+                                         stream_of(dev)), "Chan4Store")
+        del planes
+        self.chan_k = torch.empty(self.BH, self.nsb, D, self.sub, 8, dtype=torch.int32, device=dev)
+        check(lib().fathom_pack_chan4(ptr(self.code), self.BH, self.n, self.sub, ptr(self.chan_k), stream_of(dev)),
+              "Chan4Store")
+
+    def scan(self, q, act, nact, out=None, blocks=None):
+        """q [BH, G, D] fp32 -> scores fp32 [BH, G, n] over the listed channels at 4 bits; blocks=(b0, b1)
+        restricts the written range (kernels/bitplane.py:346-352)."""
+        require_cuda(q, act, nact)
+        BH, G, d = q.shape
+        dev = q.device
+        out = torch.empty(BH, G, self.n, device=dev, dtype=torch.float32) if out is None else out
+        b0, b1 = (0, _nblk(self.n)) if blocks is None else blocks
+        qc = q.contiguous().float()
+        check(lib().fathom_scan_chan4(ptr(qc), BH, G, self.n, self.sub, ptr(act.contiguous().to(torch.int32)),
+                                      ptr(nact.contiguous().to(torch.int32)), ptr(self.chan_k), ptr(self.scales_k),
+                                      b0, b1, ptr(out), stream_of(dev)), "Chan4Store.scan")
+        return out
+
+    def nbytes(self):
+        return self.chan_k.numel() * 4 + self.scales_k.numel() * 2
+
+
 def sink_local_topk(scores, k, sink=4, local=32):
     """scores [BH, G, n] -> selected indices int64 [BH, G, k] = top-(k - sink - local) among the
     non-sink / non-local tokens (score descending, ties by index ascending), then 0..sink-1, then the

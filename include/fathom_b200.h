@@ -127,6 +127,26 @@ int fathom_scan_select(const float* q, int64_t BH, int G, int64_t n, int64_t sub
                        int64_t append_local, float* scores, int64_t* out_idx, int64_t out_stride, float* out_scores,
                        void* workspace, size_t workspace_bytes, void* scan_done_event, void* stream);
 
+/* ---------------------------------------------------------------- Chan4 comparator */
+
+/* pack_chan4 (kernels/bitplane.py:67-74): codes [BH][n][128] uint8 -> chan_k [BH][nsb][128][sub][8]
+ * int32, nibble k of word m of block s = the code of token 64*(sb*sub+s) + 8*m + k (pad tokens 0). */
+int fathom_pack_chan4(const uint8_t* code, int64_t BH, int64_t n, int64_t sub, int32_t* chan_k, void* stream);
+
+/* channel_list (kernels/bitplane.py:128-132): active [BH][128] (0/1 bytes) -> act [BH][128] int32
+ * (active channels ascending, then the inactive ones ascending) and nact [BH] int32. */
+int fathom_channel_list(const uint8_t* active, int64_t BH, int32_t* act, int32_t* nact, void* stream);
+
+/* Chan4Store.scan -> scan_chan4_kernel (kernels/bitplane.py:342-352, 175-198): scores[bh][g][tok] =
+ * sum over the first nact[bh] channels of act of q[bh][g][ch] * (c - 7.5) * s / 8, reading the full
+ * 4-bit codes (32 + 2 bytes per block and channel).  q [BH][G][128] fp32, G in 1..8; chan_k from
+ * fathom_pack_chan4 and scales_k [BH][nsb][128][sub] fp16 in order `sub`; tokens of blocks
+ * [blk_begin, blk_end) are written to scores [BH][G][n], others untouched.  Channel ids are taken
+ * modulo 128 and nact clamped to 0..128. */
+int fathom_scan_chan4(const float* q, int64_t BH, int G, int64_t n, int64_t sub, const int32_t* act,
+                      const int32_t* nact, const int32_t* chan_k, const uint16_t* scales_k, int64_t blk_begin,
+                      int64_t blk_end, float* scores, void* stream);
+
 /* ---------------------------------------------------------------- selection */
 
 /* Workspace bytes fathom_select_topk / fathom_sink_local_topk need for `rows` rows of n scores:
