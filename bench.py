@@ -340,6 +340,7 @@ def hbm_figure(a, dev, bp, off, peaks, spec="config1"):
                        with_v=True)
         lay = Layer()
         lay.store = bp.PlaneStore(d["K"])
+        lay.store_K = d["K"] if (spec == "config1" and L < 4) else None
         lay.q, lay.g = d["q"], d["g"]
         lay.bytes = bp.bytes_planes(bp.make_plan(d["g"], a.budget)["t"], n)
         kvs.append((d["K"], d["V"]))
@@ -402,6 +403,7 @@ def hbm_figure(a, dev, bp, off, peaks, spec="config1"):
     torch.cuda.synchronize()
     scan_ms = f0.elapsed_time(f1) / (a.steps * len(layers))
     byts = [lay.bytes for lay in layers]
+    comparators = chan4_figure(a, bp, layers, peaks, n, BH, scores) if spec == "config1" else None
     achieved = float(np.mean(byts)) / (scan_ms * 1e-3) / 1e9
     rows = n * BH * nl
     del gs, layers, kvs
@@ -416,7 +418,42 @@ def hbm_figure(a, dev, bp, off, peaks, spec="config1"):
                                            if spec == "config1" else "not captured",
                          "bytes_per_launch": float(np.mean(byts))},
             "bits_per_row": float(np.mean(byts)) * 8 / (n * BH),
-            **({"budget_sweep": sweep} if sweep else {})}
+            **({"budget_sweep": sweep} if sweep else {}),
+            **({"chan4_comparators": comparators} if comparators else {})}
+
+
+def chan4_figure(a, bp, layers, peaks, n, BH, scores):
+    """The reference's comparator scans on the same keys (kernels/bitplane.py Chan4Store; its kernel table
+    rows): SparQ r = 16 (top-16 of sum_g |q_g|), 32 channels, and the full 4-bit scan, each a graph of scans
+    round-robin over 4 layers' stores (inputs larger than L2)."""
+    stores = [bp.Chan4Store(lay.store_K) for lay in layers[:4]]
+    out = []
+    for name, r in (("sparq_r16", 16), ("channels_32", 32), ("full_4bit", 128)):
+        lists = []
+        for lay in layers[:4]:
+            act = torch.zeros(BH, 128, dtype=torch.bool, device=lay.q.device)
+            act.scatter_(1, lay.q.abs().sum(1).topk(r, -1).indices, True)
+            lists.append(bp.channel_list(act))
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            for st, (al, nl) in zip(stores, lists):
+                st.scan(layers[0].q, al, nl, out=scores)
+        for _ in range(3):
+            g.replay()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(a.steps):
+            g.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / (a.steps * len(stores))
+        byts = float(np.mean([bp.bytes_chan4(nl, n) for _, nl in lists]))
+        out.append({"method": name, "bits_per_row": byts * 8 / (n * BH), "scan_ms_per_layer": ms,
+                    "achieved_gbs": byts / (ms * 1e-3) / 1e9, "frac_hbm": byts / (ms * 1e-3) / 1e9 / peaks["hbm_gbs"]})
+        del g
+    del stores
+    return out
 
 
 # ------------------------------------------------------------------ main
