@@ -404,6 +404,7 @@ def hbm_figure(a, dev, bp, off, peaks, spec="config1"):
     scan_ms = f0.elapsed_time(f1) / (a.steps * len(layers))
     byts = [lay.bytes for lay in layers]
     comparators = chan4_figure(a, bp, layers, peaks, n, BH, scores) if spec == "config1" else None
+    klt_step = klt_figure(a, bp, off, layers, kvs, n, BH, k_tot, scores) if spec == "config1" else None
     achieved = float(np.mean(byts)) / (scan_ms * 1e-3) / 1e9
     rows = n * BH * nl
     del gs, layers, kvs
@@ -419,7 +420,58 @@ def hbm_figure(a, dev, bp, off, peaks, spec="config1"):
                          "bytes_per_launch": float(np.mean(byts))},
             "bits_per_row": float(np.mean(byts)) * 8 / (n * BH),
             **({"budget_sweep": sweep} if sweep else {}),
-            **({"chan4_comparators": comparators} if comparators else {})}
+            **({"chan4_comparators": comparators} if comparators else {}),
+            **({"klt_step": klt_step} if klt_step else {})}
+
+
+def klt_figure(a, bp, off, layers, kvs, n, BH, k_tot, scores):
+    """The same decode step over KLT-rotated stores (planesK, scripts/R_ruler.py:63-64, 82-84): per layer
+    the query rotation + gains kernel, plan, scan + selection of the rotated queries, attention with the
+    original ones; one CUDA graph per step.  Also the one-off store build (basis + fused rotate/quantise/
+    pack) per layer."""
+    from fathom_b200 import klt
+    stores, builds = [], []
+    for L, lay in enumerate(layers):
+        K = kvs[L][0]
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        basis = klt.klt_basis(K)
+        e0.record()
+        stores.append(klt.KLTPlaneStore(K, basis))
+        e1.record()
+        e1.synchronize()
+        builds.append(e0.elapsed_time(e1))
+
+    def step():
+        for L, (lay, st) in enumerate(zip(layers, stores)):
+            qr, gains = klt.klt_query(lay.q, st.basis)
+            plan = bp.make_plan(gains, a.budget)
+            idx = bp.scan_topk(st, qr, plan, k_tot, a.sink, a.local, scores=scores)
+            off.decode_attention(lay.q, idx, kvs[L][0], kvs[L][1], n)
+
+    for _ in range(a.warmup):
+        step()
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        step()
+    for _ in range(a.warmup):
+        g.replay()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(a.steps):
+        g.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / a.steps
+    bits = []
+    for lay, st in zip(layers, stores):
+        _, gains = klt.klt_query(lay.q, st.basis)
+        bits.append(bp.bytes_planes(bp.make_plan(gains, a.budget)["t"], n) * 8 / (n * BH))
+    del g, stores
+    return {"method": f"planesK budget {a.budget:g}", "ms_per_step": ms, "bits_per_row": float(np.mean(bits)),
+            "store_build_ms_per_layer": float(np.median(builds)),
+            "extra_launches_per_layer": 1}
 
 
 def chan4_figure(a, bp, layers, peaks, n, BH, scores):

@@ -41,6 +41,8 @@ SIGNATURES = {
     "fathom_pack_chan4": (I32, [P, I64, I64, I64, P, P]),
     "fathom_channel_list": (I32, [P, I64, P, P, P]),
     "fathom_scan_chan4": (I32, [P, I64, I32, I64, I64, P, P, P, P, I64, I64, P, P]),
+    "fathom_klt_quantise_pack": (I32, [P, I32, I64, I64, I64, P, P, I64, I32, P, P, I32, P, P, P, P]),
+    "fathom_klt_query": (I32, [P, I64, I32, P, P, P, P, P]),
     "fathom_scan_select_workspace_bytes": (SZ, [I64, I32, I64, I64]),
     "fathom_scan_select": (I32, [P, I64, I32, I64, I64, P, P, I32, P, P, I64, I64, I64, I64, I64, I64, P, P, I64, P,
                                  P, SZ, P, P]),

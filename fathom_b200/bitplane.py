@@ -163,7 +163,11 @@ class PlaneStore:
     fma_cfg = {"NB": 2, "KK": 8, "num_warps": 1, "num_stages": 1}
     cls_cfg = {"NB": 4, "KK": 4, "num_warps": 1, "num_stages": 1}
 
-    def __init__(self, K, scale_dtype=torch.float16):
+    def __init__(self, K, scale_dtype=torch.float16, basis=None):
+        """basis: an optional KLT basis (fathom_b200.klt.KLTBasis: mu [BH,D], Vt [BH,D,D], lam [BH,D]).
+        Given one, the store holds the planes of (K - mu) @ Vt -- the planesK store of
+        scripts/R_ruler.py:63-64 -- built by one fused rotate + quantise + pack kernel, and scans take the
+        rotated queries q @ Vt (fathom_b200.klt.klt_query)."""
         require_cuda(K)
         self.BH, self.n, d = K.shape
         assert d == D
@@ -171,6 +175,7 @@ class PlaneStore:
             K = K.float()
         if scale_dtype not in (torch.float16, torch.float32):
             raise TypeError("PlaneStore: scale_dtype must be torch.float16 or torch.float32")
+        self.basis = None if basis is None else basis.checked(self.BH, K.device)
         self.sub = SUB
         nb = _nblk(self.n)
         self.nsb = math.ceil(nb / self.sub)
@@ -182,10 +187,17 @@ class PlaneStore:
         self._scales_blk = None
         if scale_dtype == torch.float32:        # fp32 absmax is not recoverable from the fp16 store
             self._scales_blk = torch.empty(self.BH, nb, D, dtype=torch.float32, device=dev)
-        check(lib().fathom_quantise_pack(ptr(Kc), _lib.DTYPE_CODE[Kc.dtype], self.BH, self.n, Kc.stride(0), self.sub,
-                                         int(scale_dtype == torch.float16), None, ptr(self._scales_blk),
-                                         int(scale_dtype == torch.float32), ptr(self.planes_k), ptr(self.scales_k),
-                                         stream_of(dev)), "PlaneStore")
+        if self.basis is None:
+            check(lib().fathom_quantise_pack(ptr(Kc), _lib.DTYPE_CODE[Kc.dtype], self.BH, self.n, Kc.stride(0),
+                                             self.sub, int(scale_dtype == torch.float16), None, ptr(self._scales_blk),
+                                             int(scale_dtype == torch.float32), ptr(self.planes_k), ptr(self.scales_k),
+                                             stream_of(dev)), "PlaneStore")
+        else:
+            check(lib().fathom_klt_quantise_pack(ptr(Kc), _lib.DTYPE_CODE[Kc.dtype], self.BH, self.n, Kc.stride(0),
+                                                 ptr(self.basis.mu), ptr(self.basis.Vt), self.sub,
+                                                 int(scale_dtype == torch.float16), None, ptr(self._scales_blk),
+                                                 int(scale_dtype == torch.float32), ptr(self.planes_k),
+                                                 ptr(self.scales_k), None, stream_of(dev)), "PlaneStore(basis)")
         self.planes32 = self.planes_k.view(torch.int32)
         self._code = None
 

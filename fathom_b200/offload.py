@@ -17,6 +17,7 @@ import torch
 
 from . import _lib, bitplane as bp
 from ._lib import check, lib, ptr, require_cuda, stream_of
+from .klt import klt_query
 
 _CAI_TYPESTR = {torch.int8: "|i1", torch.uint8: "|u1", torch.int16: "<i2", torch.int32: "<i4", torch.int64: "<i8",
                 torch.float16: "<f2", torch.float32: "<f4"}
@@ -106,12 +107,12 @@ class HostPlaneStore(bp.PlaneStore):
     released.  scan() reads the host memory directly (zero-copy), with the same kernel as the HBM
     store."""
 
-    def __init__(self, K, scale_dtype=torch.float16, hugepages=False):
+    def __init__(self, K, scale_dtype=torch.float16, hugepages=False, basis=None):
         require_cuda(K)
         old = bp.SUB
         try:
             bp.SUB = math.ceil(K.shape[1] / bp.BLK)
-            super().__init__(K, scale_dtype)
+            super().__init__(K, scale_dtype, basis)
         finally:
             bp.SUB = old
         self.planes_buf = MappedBuffer(self.planes_k.shape, torch.int64, K.device, hugepages)
@@ -176,9 +177,16 @@ def decode_step(q, g, budget, store, K_src, V_src, cap, k=580, sink=4, local=64,
                 V_recent=None, recent_cap=0, scores=None, out_dtype=torch.float32):
     """One layer of an offloaded decode step (offload_attn, scripts/B_e2e_offload_v2.py:180-244, planes
     method): plan -> plane-prefix scan of the (host or HBM) store -> sink+local top-k -> unique-row
-    gather + exact attention.  Returns (out [BH,G,128], idx [BH,G,k])."""
+    gather + exact attention.  Returns (out [BH,G,128], idx [BH,G,k]).
+
+    A store built with a KLT basis (planesK, scripts/R_ruler.py:82-84) is scanned with the rotated
+    queries q @ Vt and planned on their gains sum_g (q Vt)^2 * lam (g is then ignored and may be None);
+    attention always uses q itself."""
+    qs = q
+    if getattr(store, "basis", None) is not None:
+        qs, g = klt_query(q, store.basis)
     plan = bp.make_plan(g, budget)
-    idx = bp.scan_topk(store, q, plan, k, sink, local, scores=scores)
+    idx = bp.scan_topk(store, qs, plan, k, sink, local, scores=scores)
     out = decode_attention(q, idx, K_src, V_src, cap, n_host, K_recent, V_recent, recent_cap, out_dtype)
     return out, idx
 

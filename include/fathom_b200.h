@@ -147,6 +147,25 @@ int fathom_scan_chan4(const float* q, int64_t BH, int G, int64_t n, int64_t sub,
                       const int32_t* nact, const int32_t* chan_k, const uint16_t* scales_k, int64_t blk_begin,
                       int64_t blk_end, float* scores, void* stream);
 
+/* ---------------------------------------------------------------- KLT-rotated store (planesK) */
+
+/* The planesK store build (scripts/R_ruler.py:63-64: codes_u4 of einsum(Kp - mu, Vt)): the keys
+ * rotated into a per-head basis, Kr[bh][tok][e] = sum_d (K[bh][tok][d] - mu[bh][d]) * Vt[bh][d][e] in
+ * fp32 (pad tokens 0), then the same quantiser and store as fathom_quantise_pack, with the same
+ * arguments.  mu [BH][128] and Vt [BH][128][128] fp32 (Vt 16-byte aligned); rot_out, if given,
+ * receives Kr [BH][n][128] fp32 (16-byte aligned).  amax_f16 = 0 gives the reference planesK codes
+ * (codes_u4: fp32 block absmax); the stored scales_k are fp16 either way. */
+int fathom_klt_quantise_pack(const void* K, int k_dtype, int64_t BH, int64_t n, int64_t k_stride_bh,
+                             const float* mu, const float* Vt, int64_t sub, int amax_f16, uint8_t* code,
+                             void* scales_blk, int scales_blk_f32, uint64_t* planes_k, uint16_t* scales_k,
+                             float* rot_out, void* stream);
+
+/* The planesK query side (scripts/R_ruler.py:82-84): qr[bh][g][e] = sum_d q[bh][g][d] * Vt[bh][d][e]
+ * and, if gains is given, gains[bh][e] = sum_g qr[bh][g][e]^2 * lam[bh][e] (the water-filling gains of
+ * fathom_make_plan).  q [BH][G][128], lam [BH][128], qr [BH][G][128], gains [BH][128] fp32; G in 1..8. */
+int fathom_klt_query(const float* q, int64_t BH, int G, const float* Vt, const float* lam, float* qr, float* gains,
+                     void* stream);
+
 /* ---------------------------------------------------------------- selection */
 
 /* Workspace bytes fathom_select_topk / fathom_sink_local_topk need for `rows` rows of n scores:

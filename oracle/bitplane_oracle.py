@@ -249,6 +249,66 @@ def scan_scores(q, code, scales, t):
     return out
 
 
+# ---------------------------------------------------------------- KLT-rotated store (planesK)
+def klt_basis(K, skip=16):
+    """scripts/R_agent.py:59-63 (self_klt).  Keys [BH, n, D] after the first `skip` tokens (4 * SINK):
+    mu = mean, (lam, V) = eigendecomposition of the centred covariance X^T X / m (eigenvalues ascending,
+    eigenvectors as columns), lam clamped at 0.  float64; the basis is unique only up to the sign of
+    each column (and the order within equal eigenvalues)."""
+    X = np.asarray(K, np.float64)[:, skip:]
+    mu = X.mean(1)
+    Xc = X - mu[:, None]
+    C = np.einsum("hnd,hne->hde", Xc, Xc) / X.shape[1]
+    lam, V = np.linalg.eigh(C)
+    return mu, V, np.maximum(lam, 0.0)
+
+
+def klt_rotate(K, mu, Vt):
+    """scripts/R_ruler.py:63-64: (K - mu) @ Vt per head, in float64 from the fp32 difference (the
+    reference's and the CUDA path's fp32 products differ from it by summation rounding only)."""
+    X = (np.asarray(K, np.float32) - np.asarray(mu, np.float32)[:, None]).astype(np.float64)
+    return np.einsum("hnd,hde->hne", X, np.asarray(Vt, np.float64))
+
+
+def klt_rotate_bound(K, mu, Vt):
+    """|X| @ |Vt| per entry: the scale of the summation error of an fp32 rotation."""
+    X = np.abs((np.asarray(K, np.float32) - np.asarray(mu, np.float32)[:, None]).astype(np.float64))
+    return np.einsum("hnd,hde->hne", X, np.abs(np.asarray(Vt, np.float64)))
+
+
+def klt_query(q, Vt, lam):
+    """scripts/R_ruler.py:83: qr = q @ Vt (float64, rounded to fp32), gains = sum_g (qr^2 * lam) in
+    fp32, element-wise products rounded, g ascending."""
+    qr = np.einsum("hgd,hde->hge", np.asarray(q, np.float64), np.asarray(Vt, np.float64)).astype(np.float32)
+    lam = np.asarray(lam, np.float32)
+    gains = np.zeros(lam.shape, np.float32)
+    for g in range(qr.shape[1]):
+        gains = gains + (qr[:, g] * qr[:, g]) * lam
+    return qr, gains
+
+
+def allocate_layer_budgets(err, budgets, mean_target):
+    """scripts/l4_final_alloc.py:143-154 (allocate): per-layer scan budgets from a calibration table
+    err[B][L] (error of layer L at budget B).  Every layer starts at budgets[0]; while the mean budget is
+    below mean_target, the layer with the largest error drop per budget unit of its next step (first
+    layer on ties; a drop must exceed -1) moves up one step.  Returns {L: budget}."""
+    layers = list(next(iter(err.values())).keys())
+    idx = {L: 0 for L in layers}
+    while sum(budgets[i] for i in idx.values()) / len(layers) < mean_target:
+        best, best_L = -1, None
+        for L in layers:
+            i = idx[L]
+            if i + 1 >= len(budgets):
+                continue
+            d = (err[budgets[i]][L] - err[budgets[i + 1]][L]) / (budgets[i + 1] - budgets[i])
+            if d > best:
+                best, best_L = d, L
+        if best_L is None:
+            break
+        idx[best_L] += 1
+    return {L: budgets[i] for L, i in idx.items()}
+
+
 # ---------------------------------------------------------------- selection
 def topk_desc(scores, kk):
     """Largest kk per row, ordered by (score desc, index asc): the deterministic

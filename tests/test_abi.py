@@ -47,6 +47,12 @@ def test_null_and_shape_errors_are_status_codes():
                                      None) == _lib.FATHOM_ERR_UNSUPPORTED
     assert L.fathom_quantise_pack(p, 7, 1, 64, 64 * 128, 16, 1, None, None, 0, None, None, None) == \
         _lib.FATHOM_ERR_UNSUPPORTED
+    assert L.fathom_klt_quantise_pack(p, 1, 1, 64, 64 * 128, None, p, 16, 0, None, None, 0, p, p, None,
+                                      None) == _lib.FATHOM_ERR_NULL
+    assert L.fathom_klt_quantise_pack(p, 1, 1, 64, 64 * 128, p, ctypes.c_void_p(20), 16, 0, None, None, 0, p, p, None,
+                                      None) == _lib.FATHOM_ERR_SHAPE
+    assert L.fathom_klt_query(p, 2, 9, p, p, p, p, None) == _lib.FATHOM_ERR_UNSUPPORTED
+    assert L.fathom_klt_query(p, 2, 4, p, None, p, p, None) == _lib.FATHOM_ERR_NULL
 
 
 def test_python_layer_rejects_cpu_tensors():
@@ -58,6 +64,12 @@ def test_python_layer_rejects_cpu_tensors():
         bp.make_plan(torch.zeros(2, 128), 48.0)
     with pytest.raises(ValueError, match="CUDA"):
         bp.sink_local_topk(torch.zeros(2, 4, 500), 100, 4, 32)
+    from fathom_b200 import klt
+    basis = klt.KLTBasis(torch.zeros(2, 128), torch.zeros(2, 128, 128), torch.zeros(2, 128))
+    with pytest.raises(ValueError, match="CUDA"):
+        klt.klt_query(torch.zeros(2, 4, 128), basis)
+    with pytest.raises(ValueError, match="CUDA"):
+        klt.KLTPlaneStore(torch.zeros(2, 64, 128), basis)
 
 
 def test_build_entry_compiles_for_sm100a():

@@ -148,3 +148,59 @@ def test_chan4_oracle_matches_reference(c):
         assert np.array_equal(np.isinf(s), np.isinf(ref)) and np.array_equal(s[np.isinf(s)], ref[np.isinf(ref)])
         fin = np.isfinite(ref).all(-1)
         assert score_rel_err(s[fin], ref[fin]) < 1e-5
+
+
+KLT_CASES = ("k1", "k2", "k3")
+
+
+def _klt():
+    return np.load(os.path.join(os.path.dirname(__file__), "golden", "klt.npz"))
+
+
+@pytest.mark.parametrize("c", KLT_CASES)
+def test_klt_oracle_matches_reference(c):
+    """planesK (scripts/R_ruler.py:63-64, 82-84) restated against the reference's own outputs: the
+    rotation to fp32 summation rounding, the codes_u4 store bit-exact from the reference's rotated keys,
+    the query rotation and gains, the plan bit-exact from the reference's gains, the scores."""
+    z = _klt()
+    K = O.bf16_to_f32(z[f"{c}_K_bf16"].view(np.uint16))
+    mu, Vt, lam = z[f"{c}_mu"], z[f"{c}_Vt"], z[f"{c}_lam"]
+    Kr = z[f"{c}_Kr"]
+    bound = O.klt_rotate_bound(K, mu, Vt)
+    assert np.all(np.abs(O.klt_rotate(K, mu, Vt) - Kr) <= 1e-5 * bound + 1e-30)
+    code, amax = O.quantise_u4(Kr, "f32")
+    assert np.array_equal(code, z[f"{c}_code"]) and np.array_equal(amax, z[f"{c}_amax"])
+    qr, gains = O.klt_query(z[f"{c}_q"], Vt, lam)
+    qbound = np.einsum("hgd,hde->hge", np.abs(z[f"{c}_q"]).astype(np.float64), np.abs(Vt).astype(np.float64))
+    assert np.all(np.abs(qr - z[f"{c}_qr"]) <= 1e-5 * qbound + 1e-30)
+    assert np.all(np.abs(gains - z[f"{c}_gains"]) <= 1e-5 * np.abs(z[f"{c}_gains"]) + 1e-30)
+    t = O.plan_depths(z[f"{c}_gains"], float(z[f"{c}_Br"]))
+    assert np.array_equal(t.astype(np.int8), z[f"{c}_t"])
+    s = O.scan_scores(z[f"{c}_qr"], code, amax, t)
+    assert score_rel_err(s, z[f"{c}_scores"]) < 1e-5
+
+
+@pytest.mark.parametrize("c", KLT_CASES)
+def test_klt_basis_matches_reference(c):
+    """self_klt (scripts/R_agent.py:59-63): mean and covariance V diag(lam) V^T agree with the reference's
+    fp32 eigendecomposition (the basis itself is unique only up to column signs)."""
+    z = _klt()
+    K = O.bf16_to_f32(z[f"{c}_K_bf16"].view(np.uint16))
+    mu, V, lam = O.klt_basis(K)
+    assert np.abs(mu - z[f"{c}_mu"]).max() <= 1e-5 * np.abs(mu).max()
+    C = np.einsum("hde,he,hfe->hdf", V, lam, V)
+    Vr, lr = z[f"{c}_Vt"].astype(np.float64), z[f"{c}_lam"].astype(np.float64)
+    Cr = np.einsum("hde,he,hfe->hdf", Vr, lr, Vr)
+    assert np.abs(C - Cr).max() <= 1e-4 * np.abs(C).max()
+    assert np.abs(lam - lr).max() <= 1e-4 * lam.max()
+
+
+@pytest.mark.parametrize("a", ("a1", "a2", "a3"))
+def test_layer_budget_allocation_matches_reference(a):
+    """allocate (scripts/l4_final_alloc.py:143-154) on seeded error tables: identical budgets."""
+    z = _klt()
+    budgets = [int(b) for b in z[f"{a}_budgets"]]
+    E = z[f"{a}_err"]
+    err = {B: {L: float(E[i, L]) for L in range(E.shape[1])} for i, B in enumerate(budgets)}
+    alloc = O.allocate_layer_budgets(err, budgets, float(z[f"{a}_target"]))
+    assert [alloc[L] for L in range(E.shape[1])] == z[f"{a}_alloc"].tolist()
