@@ -110,36 +110,50 @@ __global__ void __launch_bounds__(KT, 2) klt_quantise_pack_kernel(
   }
 }
 
-// One CTA of 128 threads per (batch, kv-head) row; thread e owns rotated channel e.
+// Query side, latency-bound (a few KB per row): CTA (row, 32 rotated channels) of QW warps; warp w
+// sums input channels 16w .. 16w+15 for lane e (its 16 basis loads issued together), then warp 0
+// adds the QW partial sums in warp order and forms the gains.
+constexpr int QW = 8;
+constexpr int QD = D / QW;      // input channels per warp
+
 template <int G>
-__global__ void __launch_bounds__(D) klt_query_kernel(const float* __restrict__ q, const float* __restrict__ Vt,
-                                                      const float* __restrict__ lam, float* __restrict__ qr,
-                                                      float* __restrict__ gains) {
+__global__ void __launch_bounds__(QW * 32) klt_query_kernel(const float* __restrict__ q, const float* __restrict__ Vt,
+                                                            const float* __restrict__ lam, float* __restrict__ qr,
+                                                            float* __restrict__ gains) {
   __shared__ float s_q[G][D];
+  __shared__ float s_part[QW][G][32];
   const int64_t bh = blockIdx.x;
-  const int e = threadIdx.x;
+  const int e0 = blockIdx.y * 32;
+  const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
+  for (int i = tid; i < G * D; i += QW * 32) s_q[i / D][i % D] = __ldg(q + bh * G * D + i);
+  const float* V = Vt + bh * D * D + (int64_t)(w * QD) * D + e0 + lane;
+  float v[QD];
 #pragma unroll
-  for (int g = 0; g < G; ++g) s_q[g][e] = __ldg(q + (bh * G + g) * D + e);
+  for (int k = 0; k < QD; ++k) v[k] = __ldg(V + k * D);
   __syncthreads();
-  const float* V = Vt + bh * D * D + e;
   float acc[G];
 #pragma unroll
   for (int g = 0; g < G; ++g) acc[g] = 0.0f;
-#pragma unroll 8
-  for (int d = 0; d < D; ++d) {
-    const float v = __ldg(V + d * D);
 #pragma unroll
-    for (int g = 0; g < G; ++g) acc[g] = fmaf(s_q[g][d], v, acc[g]);
+  for (int k = 0; k < QD; ++k)
+#pragma unroll
+    for (int g = 0; g < G; ++g) acc[g] = fmaf(s_q[g][w * QD + k], v[k], acc[g]);
+#pragma unroll
+  for (int g = 0; g < G; ++g) s_part[w][g][lane] = acc[g];
+  __syncthreads();
+  if (w != 0) return;
+  const int e = e0 + lane;
+  const float l = gains ? __ldg(lam + bh * D + e) : 0.0f;
+  float gs = 0.0f;
+#pragma unroll
+  for (int g = 0; g < G; ++g) {
+    float s = s_part[0][g][lane];
+#pragma unroll
+    for (int ww = 1; ww < QW; ++ww) s = __fadd_rn(s, s_part[ww][g][lane]);
+    qr[(bh * G + g) * D + e] = s;
+    gs = __fadd_rn(gs, __fmul_rn(__fmul_rn(s, s), l));
   }
-#pragma unroll
-  for (int g = 0; g < G; ++g) qr[(bh * G + g) * D + e] = acc[g];
-  if (gains) {
-    const float l = __ldg(lam + bh * D + e);
-    float s = 0.0f;
-#pragma unroll
-    for (int g = 0; g < G; ++g) s = __fadd_rn(s, __fmul_rn(__fmul_rn(acc[g], acc[g]), l));
-    gains[bh * D + e] = s;
-  }
+  if (gains) gains[bh * D + e] = gs;
 }
 
 int device_sms() {
@@ -212,7 +226,7 @@ extern "C" int fathom_klt_query(const float* q, int64_t BH, int G, const float* 
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
 #define FATHOM_KLTQ(GG) \
   case GG:              \
-    klt_query_kernel<GG><<<(unsigned)BH, D, 0, st>>>(q, Vt, lam, qr, gains); \
+    klt_query_kernel<GG><<<dim3((unsigned)BH, D / 32), QW * 32, 0, st>>>(q, Vt, lam, qr, gains); \
     break;
   switch (G) {
     FATHOM_KLTQ(1)
