@@ -17,7 +17,10 @@ depends on the previous layer's output in a real model).
           by the library, right after the scan kernel), against the host link bandwidth measured in
           this run (pinned H2D cudaMemcpy, 1 GiB)
   hbm_resident  config 1 (T = 131072, index + K/V in HBM) as a secondary figure, against
-          MEASURED_PEAKS.json hbm_gbs
+          MEASURED_PEAKS.json hbm_gbs (with the Chan4 comparator scans and the KLT-store step)
+  hf_decode  end to end through a Qwen3-8B-shaped transformers model (random weights) whose attention
+          is patched onto this path, 256k-token synthetic KV cache in host memory: wall and
+          CUDA-graph device ms per generated token (`--part hf` adds 512k)
   cpu_baseline  the CPU oracle (numpy restatement of the reference path) on a bounded sample
 
 `--impl reference` times the reference's CPU path (the oracle port; the reference is Python and
@@ -62,8 +65,9 @@ def parse():
     ap.add_argument("--hbm-ctx", type=int, default=131072)
     ap.add_argument("--no-hbm", action="store_true", help="skip the HBM-resident secondary figure")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
+    ap.add_argument("--no-hf", action="store_true", help="skip the end-to-end transformers-model figure")
     ap.add_argument("--cpu-heads", type=int, default=2, help="KV heads of one layer in the CPU sample")
-    ap.add_argument("--part", choices=["all", "host", "hbm", "config3"], default="all",
+    ap.add_argument("--part", choices=["all", "host", "hbm", "config3", "hf"], default="all",
                     help="profiling runs: only the host-resident step (host) or only the HBM-resident figure (hbm)")
     return ap.parse_args()
 
@@ -508,6 +512,85 @@ def chan4_figure(a, bp, layers, peaks, n, BH, scores):
     return out
 
 
+def hf_figure(a, dev, ctxs=(262144, 524288)):
+    """End-to-end decode through a Qwen3-8B-shaped transformers model (random bf16 weights: 36 layers,
+    32 query / 8 KV heads, hidden 4096) whose attention is patched onto the offloaded path
+    (fathom_b200.hf; scripts/B_e2e_offload_v2.py), batch 1, budget a.budget, k = a.k + sink + local,
+    index and K/V rows in pinned mapped host memory.  The KV cache is synthetic (the reference's
+    --synthetic-kv mode): seeded keys and values per layer, loaded and offloaded one layer at a time.
+    Reported per context: wall ms per generated token (eager model, host-synchronised, as the
+    reference's "wall") and the device time of one step replayed from a CUDA graph (launch-free, as
+    the reference's profiler "GPU" column, paper/tables/tab_offload.tex)."""
+    from transformers import Qwen3Config, Qwen3ForCausalLM
+    from fathom_b200.hf import OffloadedDecoder
+    from fathom_b200.synth import make_layer
+    cfg = Qwen3Config(vocab_size=151936, hidden_size=4096, intermediate_size=12288, num_hidden_layers=36,
+                      num_attention_heads=32, num_key_value_heads=8, head_dim=128, rope_theta=1e6,
+                      max_position_embeddings=1 << 21, tie_word_embeddings=False, attn_implementation="sdpa")
+    old_dtype = torch.get_default_dtype()
+    torch.set_default_dtype(torch.bfloat16)
+    try:
+        with torch.device(dev):
+            torch.manual_seed(0)
+            model = Qwen3ForCausalLM(cfg).eval()
+    finally:
+        torch.set_default_dtype(old_dtype)
+    k_tot = a.k + a.sink + a.local
+    out = []
+    for n in ctxs:
+        dec = OffloadedDecoder(model, k=k_tot, sink=a.sink, local=a.local, budget=a.budget, index="host",
+                               rows="host", max_new=a.warmup + a.steps + 4)
+        try:
+            t0 = time.time()
+            for L in range(cfg.num_hidden_layers):
+                d = make_layer(cfg.num_key_value_heads, 4, n, seed=7, layer=L, device=dev, kv_dtype=torch.bfloat16,
+                               with_v=True)
+                dec.load_kv(L, d["K"].view(1, 8, n, 128), d["V"].view(1, 8, n, 128), offload=True)
+                del d
+            build_s = time.time() - t0
+            tok = torch.randint(0, cfg.vocab_size, (1, 1), device=dev)
+            for _ in range(a.warmup):
+                tok = dec.decode(tok).argmax(-1, keepdim=True)
+            torch.cuda.synchronize(dev)
+            walls = []
+            for _ in range(a.steps):
+                t1 = time.perf_counter()
+                tok = dec.decode(tok).argmax(-1, keepdim=True)
+                torch.cuda.synchronize(dev)
+                walls.append((time.perf_counter() - t1) * 1e3)
+            wall = float(np.median(walls))
+            gpu_ms, graph_note = None, None
+            try:
+                g = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(g):
+                    logits = dec.decode(tok)
+                for _ in range(3):
+                    g.replay()
+                torch.cuda.synchronize(dev)
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record()
+                for _ in range(a.steps):
+                    g.replay()
+                e1.record()
+                torch.cuda.synchronize(dev)
+                gpu_ms = e0.elapsed_time(e1) / a.steps
+                del g, logits
+            except Exception as exc:                      # capture refused by a library call: wall only
+                graph_note = f"graph capture failed: {type(exc).__name__}: {str(exc)[:120]}"
+                torch.cuda.synchronize(dev)
+            out.append({"ctx": n, "wall_ms_per_token": wall, "tok_per_s": 1e3 / wall,
+                        "gpu_ms_per_token": gpu_ms, "tok_per_s_gpu": (1e3 / gpu_ms) if gpu_ms else None,
+                        "offload_build_s": build_s, **({"note": graph_note} if graph_note else {})})
+        finally:
+            dec.free()
+            dec.unpatch()
+            torch.cuda.empty_cache()
+    del model
+    torch.cuda.empty_cache()
+    return {"model": "Qwen3-8B shape, random bf16 weights", "batch": 1, "budget": a.budget, "k": k_tot,
+            "index": "host", "rows": "host", "kv": "synthetic (seeded per layer)", "per_ctx": out}
+
+
 # ------------------------------------------------------------------ main
 def main():
     a = parse()
@@ -534,6 +617,10 @@ def main():
     if a.part == "config3":
         if rank == 0:
             print(json.dumps({"batched_hbm": hbm_figure(a, dev, bp, off, peaks, "config3")}), flush=True)
+        return
+    if a.part == "hf":
+        if rank == 0:
+            print(json.dumps({"hf_decode": hf_figure(a, dev)}), flush=True)
         return
 
     link = host_link_gbs(dev)
@@ -627,6 +714,11 @@ def main():
         torch.cuda.empty_cache()
         line["hbm_resident"] = hbm_figure(a, dev, bp, off, peaks)
         line["batched_hbm"] = hbm_figure(a, dev, bp, off, peaks, "config3")
+    if rank == 0 and world == 1 and not a.no_hf and a.part == "all":
+        try:
+            line["hf_decode"] = hf_figure(a, dev, ctxs=(262144,))
+        except Exception as exc:                          # the headline line stands without this figure
+            line["hf_decode"] = {"error": f"{type(exc).__name__}: {str(exc)[:200]}"}
     if rank == 0 and world == 1 and not a.no_cpu and a.part == "all":
         t, r = cpu_sample(a, a.cpu_heads)
         line["cpu_baseline"] = {"value": r / t, "unit": "key-rows/s", "cores": os.cpu_count(), "kind": "port",

@@ -393,10 +393,11 @@ def merge_topk(cand_scores, cand_idx, kk):
 
 # ------------------------------------------------------------------ scan + selection in one call
 def scan_select(store, q, plan, kk, mask_lo=0, mask_hi=None, index_offset=0, append_sink=0, append_local=0,
-                scores=None, with_scores=False, scan_done_event=None):
+                scores=None, with_scores=False, scan_done_event=None, idx_out=None):
     """store.scan(q, plan) and the top-kk selection of its rows in one library call.  Returns
     (idx int64 [BH, G, kk+append_sink+append_local], vals fp32 [BH, G, kk] or None, scores fp32 [BH, G, n]).
-    scan_done_event (torch.cuda.Event) is recorded right after the scan kernel."""
+    scan_done_event (torch.cuda.Event) is recorded right after the scan kernel.  idx_out: an int64
+    [BH, G, W] CUDA tensor (W >= the width) to write the indices into (its first columns); returned."""
     require_cuda(q)
     BH, G, d = q.shape
     assert BH == store.BH
@@ -405,7 +406,13 @@ def scan_select(store, q, plan, kk, mask_lo=0, mask_hi=None, index_offset=0, app
     mask_hi = n if mask_hi is None else mask_hi
     scores = torch.empty(BH, G, n, device=dev, dtype=torch.float32) if scores is None else scores
     width = kk + append_sink + append_local
-    idx = torch.empty(BH, G, width, device=dev, dtype=torch.int64)
+    if idx_out is None:
+        idx = torch.empty(BH, G, width, device=dev, dtype=torch.int64)
+    else:
+        idx = idx_out
+        if (idx.dtype != torch.int64 or idx.device != dev or idx.dim() != 3 or tuple(idx.shape[:2]) != (BH, G)
+                or idx.shape[2] < width or not idx.is_contiguous()):
+            raise ValueError(f"scan_select: idx_out must be contiguous int64 [{BH}, {G}, >= {width}] on {dev}")
     vals = torch.empty(BH, G, kk, device=dev, dtype=torch.float32) if with_scores else None
     ws = _lib.workspace(dev, lib().fathom_scan_select_workspace_bytes(BH, G, n, kk), "select")
     sub = getattr(store, "sub", None) or SUB
@@ -413,7 +420,7 @@ def scan_select(store, q, plan, kk, mask_lo=0, mask_hi=None, index_offset=0, app
     cls, clsn = plan["cls"], plan["clsn"]
     check(lib().fathom_scan_select(ptr(qc), BH, G, n, sub, ptr(cls), ptr(clsn), cls.shape[1], ptr(store.planes32),
                                    ptr(store.scales_k), kk, mask_lo, mask_hi, index_offset, append_sink, append_local,
-                                   ptr(scores), ptr(idx), width, ptr(vals), ptr(ws), ws.numel(),
+                                   ptr(scores), ptr(idx), idx.shape[2], ptr(vals), ptr(ws), ws.numel(),
                                    scan_done_event.cuda_event if scan_done_event is not None else None,
                                    stream_of(dev)),
           "scan_select")
