@@ -22,16 +22,16 @@ namespace fathom {
 namespace {
 
 constexpr int KT = 256;         // threads per CTA of the store build
-constexpr int XS = D + 4;       // row stride of the staged (K - mu) tile: 16-byte aligned rows
+constexpr int XS = QS;          // row stride of the staged (K - mu) tile: 16-byte aligned rows
 
 struct KltSmem {
   float vt[D][D];                       // basis Vt[d][e]
   union {
     float x[BLK][XS];                   // (K - mu) of the block, token-major
-    float tile[BLK][D + 1];             // rotated block, as quantise_tile reads it
+    float tile[BLK][QS];                // rotated block, as quantise_tile reads it
   } u;
   float mu[D];
-  float step[D];
+  float half_amax[2][D];
   __align__(16) uint8_t code[BLK][D];
 };
 
@@ -105,8 +105,8 @@ __global__ void __launch_bounds__(KT, 2) klt_quantise_pack_kernel(
       }
     }
     __syncthreads();
-    quantise_tile(S.u.tile, S.step, S.code, bh, blk, n, nblk, nsb, sub, amax_f16, code, scales_blk, scales_blk_f32,
-                  planes32, scales_k);
+    quantise_tile(S.u.tile, S.half_amax, S.code, bh, blk, n, nblk, nsb, sub, amax_f16, code, scales_blk,
+                  scales_blk_f32, planes32, scales_k);
   }
 }
 

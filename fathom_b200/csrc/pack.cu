@@ -9,13 +9,45 @@
 namespace fathom {
 namespace {
 
-template <typename T>
+// 16-byte vector of T -> 16 / sizeof(T) floats into the tile row
+template <typename T> struct Vec;
+template <> struct Vec<float> {
+  static constexpr int N = 4;
+  static __device__ __forceinline__ void put(const uint4& u, float* d) {
+    *reinterpret_cast<float4*>(d) = make_float4(__uint_as_float(u.x), __uint_as_float(u.y), __uint_as_float(u.z),
+                                                __uint_as_float(u.w));
+  }
+};
+template <> struct Vec<__nv_bfloat16> {
+  static constexpr int N = 8;
+  static __device__ __forceinline__ void put(const uint4& u, float* d) {
+    // bf16 -> fp32 is exact: the 16 bits become the high half
+    reinterpret_cast<float4*>(d)[0] = make_float4(__uint_as_float(u.x << 16), __uint_as_float(u.x & 0xFFFF0000u),
+                                                  __uint_as_float(u.y << 16), __uint_as_float(u.y & 0xFFFF0000u));
+    reinterpret_cast<float4*>(d)[1] = make_float4(__uint_as_float(u.z << 16), __uint_as_float(u.z & 0xFFFF0000u),
+                                                  __uint_as_float(u.w << 16), __uint_as_float(u.w & 0xFFFF0000u));
+  }
+};
+template <> struct Vec<__half> {
+  static constexpr int N = 8;
+  static __device__ __forceinline__ void put(const uint4& u, float* d) {
+    const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&u.x));
+    const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&u.y));
+    const float2 c = __half22float2(*reinterpret_cast<const __half2*>(&u.z));
+    const float2 e = __half22float2(*reinterpret_cast<const __half2*>(&u.w));
+    reinterpret_cast<float4*>(d)[0] = make_float4(a.x, a.y, b.x, b.y);
+    reinterpret_cast<float4*>(d)[1] = make_float4(c.x, c.y, e.x, e.y);
+  }
+};
+
+// VEC: the tile is read with 16-byte loads (every row 16-byte aligned: checked by the launcher).
+template <typename T, bool VEC>
 __global__ void __launch_bounds__(256) quantise_pack_kernel(
     const T* __restrict__ K, int64_t n, int64_t k_stride_bh, int64_t nblk, int64_t nsb, int64_t sub, int amax_f16,
     uint8_t* __restrict__ code, void* __restrict__ scales_blk, int scales_blk_f32, uint32_t* __restrict__ planes32,
     uint16_t* __restrict__ scales_k) {
-  __shared__ float tile[BLK][D + 1];
-  __shared__ float s_step[D];
+  __shared__ __align__(16) float tile[BLK][QS];
+  __shared__ float s_half[2][D];
   __shared__ __align__(16) uint8_t s_code[BLK][D];
 
   const int64_t blk = blockIdx.x;
@@ -25,14 +57,33 @@ __global__ void __launch_bounds__(256) quantise_pack_kernel(
   const int64_t tok0 = blk * BLK;
   const T* Kb = K + bh * k_stride_bh;
 
-  for (int e = tid; e < BLK * D; e += blockDim.x) {
-    const int r = e >> 7, c = e & (D - 1);
-    const int64_t tok = tok0 + r;
-    tile[r][c] = (real_blk && tok < n) ? load_elem<T>(Kb + tok * D + c) : 0.0f;
+  if (VEC) {
+    constexpr int NV = Vec<T>::N;            // elements per 16-byte vector
+    constexpr int VPR = D / NV;              // vectors per row
+    constexpr int PER = BLK * VPR / 256;     // vectors per thread
+    uint4 u[PER];
+#pragma unroll
+    for (int k = 0; k < PER; ++k) {          // all loads in flight before any use
+      const int e = tid + k * 256;
+      const int r = e / VPR, cv = e % VPR;
+      const int64_t tok = tok0 + r;
+      u[k] = (real_blk && tok < n) ? __ldg(reinterpret_cast<const uint4*>(Kb + tok * D) + cv) : make_uint4(0, 0, 0, 0);
+    }
+#pragma unroll
+    for (int k = 0; k < PER; ++k) {
+      const int e = tid + k * 256;
+      Vec<T>::put(u[k], &tile[e / VPR][(e % VPR) * NV]);
+    }
+  } else {
+    for (int e = tid; e < BLK * D; e += blockDim.x) {
+      const int r = e >> 7, c = e & (D - 1);
+      const int64_t tok = tok0 + r;
+      tile[r][c] = (real_blk && tok < n) ? load_elem<T>(Kb + tok * D + c) : 0.0f;
+    }
   }
   __syncthreads();
 
-  quantise_tile(tile, s_step, s_code, bh, blk, n, nblk, nsb, sub, amax_f16, code, scales_blk, scales_blk_f32,
+  quantise_tile(tile, s_half, s_code, bh, blk, n, nblk, nsb, sub, amax_f16, code, scales_blk, scales_blk_f32,
                 planes32, scales_k);
 }
 
@@ -148,24 +199,31 @@ extern "C" int fathom_quantise_pack(const void* K, int k_dtype, int64_t BH, int6
   dim3 grid((unsigned)grid_blocks, (unsigned)BH);
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   uint32_t* p32 = reinterpret_cast<uint32_t*>(planes_k);
+  const bool vec = (reinterpret_cast<uintptr_t>(K) & 15) == 0;
+#define FATHOM_QP(TT)                                                                                                \
+  {                                                                                                                 \
+    const TT* Kt = static_cast<const TT*>(K);                                                                       \
+    if (vec && (k_stride_bh * (int64_t)sizeof(TT)) % 16 == 0)                                                       \
+      quantise_pack_kernel<TT, true><<<grid, 256, 0, st>>>(Kt, n, k_stride_bh, nblk, nsb, sub, amax_f16, code,      \
+                                                           scales_blk, scales_blk_f32, p32, scales_k);              \
+    else                                                                                                            \
+      quantise_pack_kernel<TT, false><<<grid, 256, 0, st>>>(Kt, n, k_stride_bh, nblk, nsb, sub, amax_f16, code,     \
+                                                            scales_blk, scales_blk_f32, p32, scales_k);             \
+  }
   switch (k_dtype) {
     case FATHOM_DTYPE_F32:
-      quantise_pack_kernel<float><<<grid, 256, 0, st>>>(static_cast<const float*>(K), n, k_stride_bh, nblk, nsb, sub,
-                                                        amax_f16, code, scales_blk, scales_blk_f32, p32, scales_k);
+      FATHOM_QP(float)
       break;
     case FATHOM_DTYPE_BF16:
-      quantise_pack_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>(static_cast<const __nv_bfloat16*>(K), n, k_stride_bh,
-                                                                nblk, nsb, sub, amax_f16, code, scales_blk,
-                                                                scales_blk_f32, p32, scales_k);
+      FATHOM_QP(__nv_bfloat16)
       break;
     case FATHOM_DTYPE_F16:
-      quantise_pack_kernel<__half><<<grid, 256, 0, st>>>(static_cast<const __half*>(K), n, k_stride_bh, nblk, nsb,
-                                                         sub, amax_f16, code, scales_blk, scales_blk_f32, p32,
-                                                         scales_k);
+      FATHOM_QP(__half)
       break;
     default:
       return set_error(FATHOM_ERR_UNSUPPORTED, "quantise_pack: unknown k_dtype %d", k_dtype);
   }
+#undef FATHOM_QP
   return check_launch("quantise_pack");
 }
 

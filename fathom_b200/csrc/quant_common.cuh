@@ -29,55 +29,66 @@ __device__ __forceinline__ int code_of(float x, float s) {
   return (int)f + 8;
 }
 
+constexpr int QS = D + 4;        // row stride of a staged tile: 16-byte aligned rows, conflict-free columns
+
 // Block scales, codes and plane words of the staged tile (tile[r][c] = value of token 64*blk + r,
-// channel c; pad tokens hold 0).  Called by all 256 threads of the CTA; only reads the tile.  Writes
-// scales_blk / scales_k / planes32 / code where given.  Ends after a barrier only when `code` is
-// written, so a caller that re-stages the tile must synchronise first.
-__device__ __forceinline__ void quantise_tile(const float (*tile)[D + 1], float* s_step, uint8_t (*s_code)[D],
+// channel c; pad tokens hold 0).  Called by all 256 threads of the CTA; thread (c, h) owns channel c
+// and the 32 tokens of half h: its 32 values are read once into registers (column reads, conflict-free
+// with the QS stride), the two halves' absmax meet in s_half, and the thread forms its four 32-bit
+// plane half-words in registers.  Writes scales_blk / scales_k / planes32 / code where given.  Ends
+// after a barrier only when `code` is written, so a caller that re-stages the tile (or s_half)
+// must synchronise first.
+__device__ __forceinline__ void quantise_tile(const float (*tile)[QS], float (*s_half)[D], uint8_t (*s_code)[D],
                                               int64_t bh, int64_t blk, int64_t n, int64_t nblk, int64_t nsb,
                                               int64_t sub, int amax_f16, uint8_t* __restrict__ code,
                                               void* __restrict__ scales_blk, int scales_blk_f32,
                                               uint32_t* __restrict__ planes32, uint16_t* __restrict__ scales_k) {
   const int tid = threadIdx.x;
+  const int j = tid & (D - 1), h = tid >> 7;
   const bool real_blk = blk < nblk;
   const int64_t tok0 = blk * BLK;
   const int64_t sb = blk / sub, s_in = blk - sb * sub;
-  if (tid < D) {
-    float a = 0.0f;
-#pragma unroll 8
-    for (int r = 0; r < BLK; ++r) a = fmaxf(a, fabsf(tile[r][tid]));
-    a = fmaxf(a, 1e-8f);
-    const __half a16 = __float2half_rn(a);
-    const float aq = amax_f16 ? __half2float(a16) : a;
-    s_step[tid] = aq * 0.125f;  // exact: power-of-two scaling
+  float v[32];
+  float a = 0.0f;
+#pragma unroll
+  for (int i = 0; i < 32; ++i) {
+    v[i] = tile[h * 32 + i][j];
+    a = fmaxf(a, fabsf(v[i]));
+  }
+  s_half[h][j] = a;
+  __syncthreads();
+  a = fmaxf(fmaxf(s_half[0][j], s_half[1][j]), 1e-8f);
+  const __half a16 = __float2half_rn(a);
+  const float aq = amax_f16 ? __half2float(a16) : a;
+  const float step = aq * 0.125f;  // exact: power-of-two scaling
+  if (h == 0) {
     if (real_blk && scales_blk) {
-      const int64_t o = (bh * nblk + blk) * D + tid;
+      const int64_t o = (bh * nblk + blk) * D + j;
       if (scales_blk_f32) reinterpret_cast<float*>(scales_blk)[o] = aq;
       else reinterpret_cast<__half*>(scales_blk)[o] = a16;
     }
-    if (scales_k) scales_k[((bh * nsb + sb) * D + tid) * sub + s_in] = real_blk ? __half_as_ushort(a16) : (uint16_t)0;
+    if (scales_k) scales_k[((bh * nsb + sb) * D + j) * sub + s_in] = real_blk ? __half_as_ushort(a16) : (uint16_t)0;
   }
-  __syncthreads();
-
-  const int warp = tid >> 5, lane = tid & 31;
-  const int h = warp & 1;           // token half of the block: tokens 32h .. 32h+31
-  const int c0 = (warp >> 1) * 32;  // 32 channels per warp pair
-  const int r = h * 32 + lane;
-  const bool tok_ok = real_blk && (tok0 + r) < n;
-  for (int jj = 0; jj < 32; ++jj) {
-    const int j = c0 + jj;
-    const int c = tok_ok ? code_of(tile[r][j], s_step[j]) : 0;
-    s_code[r][j] = (uint8_t)c;
-    if (planes32) {
-      const uint32_t b0 = __ballot_sync(0xffffffffu, (c >> 3) & 1);
-      const uint32_t b1 = __ballot_sync(0xffffffffu, (c >> 2) & 1);
-      const uint32_t b2 = __ballot_sync(0xffffffffu, (c >> 1) & 1);
-      const uint32_t b3 = __ballot_sync(0xffffffffu, c & 1);
-      if (lane < NPLANES) {
-        const uint32_t b = lane == 0 ? b0 : lane == 1 ? b1 : lane == 2 ? b2 : b3;
-        planes32[((((bh * nsb + sb) * D + j) * NPLANES + lane) * sub + s_in) * 2 + h] = b;
-      }
-    }
+  // tokens of this half that exist: pad tokens (and pad blocks) have code 0
+  const int64_t rem = real_blk ? n - (tok0 + h * 32) : 0;
+  const int live = rem <= 0 ? 0 : (rem >= 32 ? 32 : (int)rem);
+  uint32_t w0 = 0, w1 = 0, w2 = 0, w3 = 0;
+#pragma unroll
+  for (int i = 0; i < 32; ++i) {
+    const uint32_t c = i < live ? (uint32_t)code_of(v[i], step) : 0u;
+    w0 |= ((c >> 3) & 1u) << i;
+    w1 |= ((c >> 2) & 1u) << i;
+    w2 |= ((c >> 1) & 1u) << i;
+    w3 |= (c & 1u) << i;
+    if (code) s_code[h * 32 + i][j] = (uint8_t)c;
+  }
+  if (planes32) {
+    uint32_t* o = planes32 + ((((bh * nsb + sb) * D + j) * NPLANES) * sub + s_in) * 2 + h;
+    const int64_t ps = sub * 2;     // words between consecutive planes of one (block, channel)
+    o[0] = w0;
+    o[ps] = w1;
+    o[2 * ps] = w2;
+    o[3 * ps] = w3;
   }
   if (code && real_blk) {
     __syncthreads();
