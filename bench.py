@@ -19,7 +19,7 @@ depends on the previous layer's output in a real model).
   hbm_resident  config 1 (T = 131072, index + K/V in HBM) as a secondary figure, against
           MEASURED_PEAKS.json hbm_gbs (with the Chan4 comparator scans and the KLT-store step)
   hf_decode  end to end through a Qwen3-8B-shaped transformers model (random weights) whose attention
-          is patched onto this path, 256k-token synthetic KV cache in host memory: wall and
+          is patched onto this path, synthetic KV cache in host memory at 256k and 1M tokens: wall and
           CUDA-graph device ms per generated token (`--part hf` adds 512k)
   cpu_baseline  the CPU oracle (numpy restatement of the reference path) on a bounded sample
 
@@ -66,7 +66,7 @@ def parse():
     ap.add_argument("--no-hbm", action="store_true", help="skip the HBM-resident secondary figure")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
     ap.add_argument("--no-hf", action="store_true", help="skip the end-to-end transformers-model figure")
-    ap.add_argument("--hf-ctx", default="", help="--part hf: comma-separated context lengths (default 262144,524288)")
+    ap.add_argument("--hf-ctx", default="", help="--part hf: comma-separated context lengths (default 256k, 512k, 1M)")
     ap.add_argument("--cpu-heads", type=int, default=2, help="KV heads of one layer in the CPU sample")
     ap.add_argument("--part", choices=["all", "host", "hbm", "config3", "hf"], default="all",
                     help="profiling runs: only the host-resident step (host) or only the HBM-resident figure (hbm)")
@@ -538,6 +538,20 @@ def chan4_figure(a, bp, layers, peaks, n, BH, scores):
     return out
 
 
+def hf_row_buffers(ctx, layers, hkv):
+    """Distinct K/V row buffers the host can pin for the model figure: every layer's own when they fit
+    in 45% of the available memory, else 4 shared round-robin (each layer still has its own index)."""
+    avail = 0
+    try:
+        for line in open("/proc/meminfo"):
+            if line.startswith("MemAvailable:"):
+                avail = int(line.split()[1]) * 1024
+    except OSError:
+        pass
+    per_layer = hkv * ctx * 512 + hkv * 128 * (-(-ctx // 64)) * 34      # rows + index
+    return layers if avail == 0 or layers * per_layer <= 0.45 * avail else 4
+
+
 def hf_figure(a, dev, ctxs=(262144, 524288)):
     """End-to-end decode through a Qwen3-8B-shaped transformers model (random bf16 weights: 36 layers,
     32 query / 8 KV heads, hidden 4096) whose attention is patched onto the offloaded path
@@ -568,10 +582,12 @@ def hf_figure(a, dev, ctxs=(262144, 524288)):
                                rows="host", max_new=a.warmup + a.steps + 4)
         try:
             t0 = time.time()
+            nrows = hf_row_buffers(n, cfg.num_hidden_layers, cfg.num_key_value_heads)
             for L in range(cfg.num_hidden_layers):
                 d = make_layer(cfg.num_key_value_heads, 4, n, seed=7, layer=L, device=dev, kv_dtype=torch.bfloat16,
-                               with_v=True)
-                dec.load_kv(L, d["K"].view(1, 8, n, 128), d["V"].view(1, 8, n, 128), offload=True)
+                               with_v=L < nrows)
+                dec.load_kv(L, d["K"].view(1, 8, n, 128), d["V"].view(1, 8, n, 128) if L < nrows else None,
+                            offload=True, rows_of=None if L < nrows else L % nrows)
                 del d
             build_s = time.time() - t0
             tok = torch.randint(0, cfg.vocab_size, (1, 1), device=dev)
@@ -610,7 +626,8 @@ def hf_figure(a, dev, ctxs=(262144, 524288)):
                 torch.cuda.synchronize(dev)
             out.append({"ctx": n, "wall_ms_per_token": wall, "tok_per_s": 1e3 / wall,
                         "gpu_ms_per_token": gpu_ms, "tok_per_s_gpu": (1e3 / gpu_ms) if gpu_ms else None,
-                        "offload_build_s": build_s, **({"note": graph_note} if graph_note else {})})
+                        "offload_build_s": build_s, "row_buffers": nrows,
+                        **({"note": graph_note} if graph_note else {})})
         finally:
             dec.free()
             dec.unpatch()
@@ -650,7 +667,7 @@ def main():
         return
     if a.part == "hf":
         if rank == 0:
-            ctxs = tuple(int(x) for x in a.hf_ctx.split(",")) if a.hf_ctx else (262144, 524288)
+            ctxs = tuple(int(x) for x in a.hf_ctx.split(",")) if a.hf_ctx else (262144, 524288, 1048576)
             print(json.dumps({"hf_decode": hf_figure(a, dev, ctxs)}), flush=True)
         return
 
@@ -752,7 +769,7 @@ def main():
         line["batched_hbm"] = hbm_figure(a, dev, bp, off, peaks, "config3")
     if rank == 0 and world == 1 and not a.no_hf and a.part == "all":
         try:
-            line["hf_decode"] = hf_figure(a, dev, ctxs=(262144,))
+            line["hf_decode"] = hf_figure(a, dev, ctxs=(262144, 1048576))
         except Exception as exc:                          # the headline line stands without this figure
             line["hf_decode"] = {"error": f"{type(exc).__name__}: {str(exc)[:200]}"}
     if rank == 0 and world == 1 and not a.no_cpu and a.part == "all":

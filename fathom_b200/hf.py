@@ -150,16 +150,18 @@ class OffloadedDecoder:
         mask = torch.arange(m, device=q.device)[None] <= (m0 + torch.arange(Tq, device=q.device))[:, None]
         return F.scaled_dot_product_attention(q, c.Kdev[:, :, :m], c.Vdev[:, :, :m], attn_mask=mask, enable_gqa=True)
 
-    def load_kv(self, L, K, V, offload=False):
+    def load_kv(self, L, K, V, offload=False, rows_of=None):
         """Install prefill keys/values [B, Hkv, n, D] for layer L without running the model (the
         reference's --synthetic-kv mode, :280-283); offload=True builds the layer's stores at once, so
-        only one layer's prefill K/V is ever on the device."""
+        only one layer's prefill K/V is ever on the device.  rows_of=L0 (< L, already offloaded): the
+        layer's index is built from K, but attention reads layer L0's row buffers (V unused) -- for
+        timing runs whose host memory cannot hold every layer's rows."""
         if L == 0:
             self._reset(K.shape[0])
         c = self.cache[L]
         c.Kdev, c.Vdev, c.len = K, V, K.shape[2]
         if offload:
-            self._offload_layer(L)
+            self._offload_layer(L, rows_of)
             if L == len(self.cache) - 1:
                 self._finish_offload()
 
@@ -170,7 +172,7 @@ class OffloadedDecoder:
             self._offload_layer(L)
         self._finish_offload()
 
-    def _offload_layer(self, L):
+    def _offload_layer(self, L, rows_of=None):
         B, Hkv, D = self.B, self.Hkv, self.D
         BH = B * Hkv
         c = self.cache[L]
@@ -180,7 +182,7 @@ class OffloadedDecoder:
         if L > 0 and n != self.cache[0].n:
             raise ValueError("OffloadedDecoder: every layer needs the same prefill length")
         K = c.Kdev[:, :, :n].reshape(BH, n, D).to(torch.bfloat16)
-        V = c.Vdev[:, :, :n].reshape(BH, n, D).to(torch.bfloat16)
+        V = None if rows_of is not None else c.Vdev[:, :, :n].reshape(BH, n, D).to(torch.bfloat16)
         dev = K.device
         basis = klt_mod.klt_basis(K) if self.klt else None
         if self.index == "host":
@@ -189,7 +191,12 @@ class OffloadedDecoder:
         else:
             c.store = klt_mod.KLTPlaneStore(K, basis) if self.klt else bp.PlaneStore(K)
         c.var = None if self.klt else K[:, SKIP:].float().var(1)
-        if self.rows == "host":
+        if rows_of is not None:
+            src = self.cache[rows_of]
+            if not (0 <= rows_of < L) or src.K_src is None or src.n != n:
+                raise ValueError(f"OffloadedDecoder: rows_of={rows_of} must name an offloaded earlier layer")
+            c.K_src, c.V_src = src.K_src, src.V_src
+        elif self.rows == "host":
             buf = MappedBuffer((BH, n, 2 * D), torch.bfloat16, dev)
             buf.dev[..., :D].copy_(K)
             buf.dev[..., D:].copy_(V)

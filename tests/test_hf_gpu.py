@@ -122,3 +122,36 @@ def test_decode_attention_layer_vs_oracle(index, rows, klt):
     finally:
         dec.free()
         dec.unpatch()
+
+
+@pytest.mark.parametrize("klt", [False, True])
+def test_qwen2_without_qk_norm(klt):
+    """A Qwen2-family model (no QK-norm, biased q/k/v projections; the case the KLT index is for):
+    with k covering the whole context the patched decode matches the unpatched model's decode."""
+    from transformers import Qwen2Config, Qwen2ForCausalLM
+    from fathom_b200.hf import OffloadedDecoder
+    torch.manual_seed(3)
+    cfg = Qwen2Config(vocab_size=512, hidden_size=1024, intermediate_size=512, num_hidden_layers=2,
+                      num_attention_heads=8, num_key_value_heads=2, head_dim=128, max_position_embeddings=8192,
+                      attn_implementation="sdpa")
+    model = Qwen2ForCausalLM(cfg).to("cuda", torch.bfloat16).eval()
+    B, n, steps = 1, 1200, 2
+    ids = torch.randint(0, 512, (B, n + steps), device="cuda", generator=torch.Generator("cuda").manual_seed(4))
+    with torch.no_grad():
+        out = model(ids[:, :n], use_cache=True)
+        past, ref = out.past_key_values, []
+        for s in range(steps):
+            o = model(ids[:, n + s:n + s + 1], past_key_values=past, use_cache=True)
+            past = o.past_key_values
+            ref.append(o.logits[:, -1])
+    dec = OffloadedDecoder(model, k=600, index="host", rows="host", klt=klt, max_new=4, prefill_chunk=512)
+    try:
+        dec.prefill(ids[:, :n])
+        dec.offload()
+        for s in range(steps):
+            dec.k = dec.context + 1
+            logits = dec.decode(ids[:, n + s:n + s + 1])
+            assert _close(logits, ref[s], 3e-2), s
+    finally:
+        dec.free()
+        dec.unpatch()
