@@ -121,7 +121,7 @@ __global__ void __launch_bounds__(HT, 2) collect_kernel(const float* __restrict_
   const bool unmasked = i0 >= mask_lo && i1 <= mask_hi;   // the whole chunk is outside sink/local
 #pragma unroll 1
   for (int round = 0; round < 2; ++round) {
-    // thread t owns scores i0 + 4t + 4*HT*u + e; this round's loads first, then the filter
+    // thread t owns scores i0 + 4t + 4*HT*u + e; this pass's loads first, then the filter
     float x[HALF];
 #pragma unroll
     for (int uu = 0; uu < HALF / 4; ++uu) {
