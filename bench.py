@@ -558,9 +558,10 @@ def hf_figure(a, dev, ctxs=(262144, 524288)):
     (fathom_b200.hf; scripts/B_e2e_offload_v2.py), batch 1, budget a.budget, k = a.k + sink + local,
     index and K/V rows in pinned mapped host memory.  The KV cache is synthetic (the reference's
     --synthetic-kv mode): seeded keys and values per layer, loaded and offloaded one layer at a time.
-    Reported per context: wall ms per generated token (eager model, host-synchronised, as the
-    reference's "wall") and the device time of one step replayed from a CUDA graph (launch-free, as
-    the reference's profiler "GPU" column, paper/tables/tab_offload.tex)."""
+    Reported per context: wall ms per generated token with the model run eagerly (host-synchronised,
+    as the reference's "wall"), wall ms per token in graph mode (OffloadedDecoder(graphs=True): one
+    captured step replayed per token), and the device time of that step replayed back to back
+    (launch-free, as the reference's profiler "GPU" column, paper/tables/tab_offload.tex)."""
     from transformers import Qwen3Config, Qwen3ForCausalLM
     from fathom_b200.hf import OffloadedDecoder
     from fathom_b200.synth import make_layer
@@ -579,7 +580,7 @@ def hf_figure(a, dev, ctxs=(262144, 524288)):
     out = []
     for n in ctxs:
         dec = OffloadedDecoder(model, k=k_tot, sink=a.sink, local=a.local, budget=a.budget, index="host",
-                               rows="host", max_new=a.warmup + a.steps + 4)
+                               rows="host", max_new=a.local + 2 * (a.warmup + a.steps) + 8, graphs=True)
         try:
             t0 = time.time()
             nrows = hf_row_buffers(n, cfg.num_hidden_layers, cfg.num_key_value_heads)
@@ -605,26 +606,32 @@ def hf_figure(a, dev, ctxs=(262144, 524288)):
                 if i == 0:
                     torch.cuda.profiler.stop()
             wall = float(np.median(walls))
-            gpu_ms, graph_note = None, None
-            try:
-                g = torch.cuda.CUDAGraph()
-                with torch.cuda.graph(g):
-                    logits = dec.decode(tok)
-                for _ in range(3):
-                    g.replay()
+            # graph mode: eager steps until the local window lies in the recent buffer, then one captured
+            # step replayed per token (OffloadedDecoder(graphs=True)); wall per token, host-synchronised
+            while dec.cache[0].nrec + 1 < a.local:
+                tok = dec.decode(tok).argmax(-1, keepdim=True)
+            for _ in range(a.warmup):
+                tok = dec.decode(tok).argmax(-1, keepdim=True)
+            torch.cuda.synchronize(dev)
+            gwalls = []
+            for _ in range(a.steps):
+                t1 = time.perf_counter()
+                tok = dec.decode(tok).argmax(-1, keepdim=True)
                 torch.cuda.synchronize(dev)
-                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-                e0.record()
-                for _ in range(a.steps):
-                    g.replay()
-                e1.record()
-                torch.cuda.synchronize(dev)
-                gpu_ms = e0.elapsed_time(e1) / a.steps
-                del g, logits
-            except Exception as exc:                      # capture refused by a library call: wall only
-                graph_note = f"graph capture failed: {type(exc).__name__}: {str(exc)[:120]}"
-                torch.cuda.synchronize(dev)
+                gwalls.append((time.perf_counter() - t1) * 1e3)
+            graph_wall = float(np.median(gwalls))
+            # device time of one step: the captured graph replayed back to back
+            g = dec._graph
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for _ in range(a.steps):
+                g.replay()
+            e1.record()
+            torch.cuda.synchronize(dev)
+            gpu_ms = e0.elapsed_time(e1) / a.steps
+            graph_note = None
             out.append({"ctx": n, "wall_ms_per_token": wall, "tok_per_s": 1e3 / wall,
+                        "graph_wall_ms_per_token": graph_wall, "tok_per_s_graph": 1e3 / graph_wall,
                         "gpu_ms_per_token": gpu_ms, "tok_per_s_gpu": (1e3 / gpu_ms) if gpu_ms else None,
                         "offload_build_s": build_s, "row_buffers": nrows,
                         **({"note": graph_note} if graph_note else {})})

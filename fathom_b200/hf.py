@@ -56,10 +56,15 @@ class OffloadedDecoder:
                     for the K/V rows
     max_new         capacity of the recent-token buffer (generated tokens)
     klt             KLT-rotated index (planesK) instead of the plain one
+    graphs          replay one CUDA graph of the whole model step per generated token once the local
+                    window lies inside the recent-token buffer (from the local-th generated token on;
+                    the steps before run eagerly): the slot of the new token, the window's first index
+                    and the position are then device-resident inputs, so one capture serves every
+                    later step
     """
 
     def __init__(self, model, k=580, sink=4, local=64, budget=48.0, index="host", rows="host", max_new=64,
-                 klt=False, prefill_chunk=2048):
+                 klt=False, prefill_chunk=2048, graphs=False):
         cfg = model.config
         self.model = model
         self.Hq = cfg.num_attention_heads
@@ -88,6 +93,10 @@ class OffloadedDecoder:
         self.cache = [_Layer() for _ in range(nL)]
         self._orig = {}
         self._scores = self._idx = self._arange_local = None
+        self.graphs = graphs
+        self._graph = self._graph_logits = None
+        self._graph_mode = False
+        self._ids_s = self._pos_s = self._slot_s = self._wbase_s = None
         for L, m in enumerate(self.attn):
             self._orig[L] = m.forward
             m.forward = types.MethodType(self._make_forward(L), m)
@@ -216,6 +225,12 @@ class OffloadedDecoder:
         self._scores = torch.empty(BH, self.G, n, dtype=torch.float32, device=dev)
         self._idx = torch.empty(BH, self.G, self.k, dtype=torch.int64, device=dev)
         self._arange_local = torch.arange(self.local, dtype=torch.int64, device=dev)
+        # graph-mode inputs: token ids, positions, the recent-buffer slot, the local window's first index
+        self._ids_s = torch.zeros(self.B, 1, dtype=torch.long, device=dev)
+        self._pos_s = torch.zeros(self.B, 1, dtype=torch.long, device=dev)
+        self._slot_s = torch.zeros(1, dtype=torch.long, device=dev)
+        self._wbase_s = torch.zeros((), dtype=torch.long, device=dev)
+        self._graph = self._graph_logits = None
         torch.cuda.synchronize(dev)
         self.mode = "decode"
 
@@ -225,7 +240,8 @@ class OffloadedDecoder:
         self.cache = [_Layer() for _ in self.attn]
 
     def free(self):
-        """Release the host buffers of the current batch."""
+        """Release the host buffers of the current batch (and the captured graph)."""
+        self._graph = self._graph_logits = None
         for c in self.cache:
             for o in c.owned:
                 o.free()
@@ -247,9 +263,42 @@ class OffloadedDecoder:
             raise RuntimeError("OffloadedDecoder: decode() needs offload() of a batch of the same size")
         if self.cache[0].nrec >= self.max_new:
             raise RuntimeError(f"OffloadedDecoder: recent-token buffer full ({self.max_new} tokens)")
+        if self.graphs and self.cache[0].nrec + 1 >= self.local:
+            return self._decode_graph(input_ids)
         pos = torch.full((B, 1), self.context, device=input_ids.device, dtype=torch.long)
         with torch.no_grad():
             return self.model(input_ids, position_ids=pos, use_cache=False).logits[:, -1]
+
+    def _decode_graph(self, input_ids):
+        """One step by graph replay (captured on first use).  From here on the masked prefill tail is
+        empty (min(n, m - local) = n), so the captured launches differ from step to step only in the
+        device-resident inputs set below."""
+        c0 = self.cache[0]
+        r = c0.nrec
+        self._ids_s.copy_(input_ids)
+        self._pos_s.fill_(c0.n + r)
+        self._slot_s.fill_(r)
+        self._wbase_s.fill_(c0.n + r + 1 - self.local)
+        if self._graph is None:
+            self._graph_mode = True
+            try:
+                with torch.no_grad():
+                    side = torch.cuda.Stream(device=input_ids.device)
+                    side.wait_stream(torch.cuda.current_stream(input_ids.device))
+                    with torch.cuda.stream(side):       # warm-up run of this very step, then the capture
+                        self.model(self._ids_s, position_ids=self._pos_s, use_cache=False)
+                    torch.cuda.current_stream(input_ids.device).wait_stream(side)
+                    g = torch.cuda.CUDAGraph()
+                    with torch.cuda.graph(g):
+                        self._graph_logits = self.model(self._ids_s, position_ids=self._pos_s,
+                                                        use_cache=False).logits[:, -1]
+                self._graph = g
+            finally:
+                self._graph_mode = False
+        self._graph.replay()
+        for c in self.cache:
+            c.nrec = r + 1
+        return self._graph_logits.clone()
 
     def _decode_attn(self, L, q, k, v):
         c = self.cache[L]
@@ -257,13 +306,19 @@ class OffloadedDecoder:
         if Tq != 1:
             raise RuntimeError("OffloadedDecoder: decode takes one token per sequence")
         BH, G = B * self.Hkv, self.G
-        r = c.nrec
-        c.Krec[:, r] = k.reshape(BH, D)
-        c.Vrec[:, r] = v.reshape(BH, D)
-        c.nrec = r + 1
-        n, m = c.n, c.n + c.nrec
         sink, local = self.sink, self.local
         kk = self.k - sink - local
+        n = c.n
+        if self._graph_mode:                     # slot and window base are device inputs; nrec moves outside
+            c.Krec.index_copy_(1, self._slot_s, k.reshape(BH, 1, D))
+            c.Vrec.index_copy_(1, self._slot_s, v.reshape(BH, 1, D))
+            m = n + c.nrec + 1
+        else:
+            r = c.nrec
+            c.Krec[:, r] = k.reshape(BH, D)
+            c.Vrec[:, r] = v.reshape(BH, D)
+            c.nrec = r + 1
+            m = n + c.nrec
         hi = min(n, m - local)
         if hi - sink < kk:
             raise ValueError(f"OffloadedDecoder: {hi - sink} selectable prefill tokens < k - sink - local = {kk}")
@@ -279,7 +334,8 @@ class OffloadedDecoder:
         bp.scan_select(c.store, qs, plan, kk, mask_lo=sink, mask_hi=hi, append_sink=sink, scores=self._scores,
                        idx_out=idx)
         # the local window [m - local, m): one add into the strided tail of the index rows
-        torch.add(self._arange_local.expand(BH, G, local), m - local, out=idx[..., kk + sink:])
+        torch.add(self._arange_local.expand(BH, G, local), self._wbase_s if self._graph_mode else m - local,
+                  out=idx[..., kk + sink:])
         out = decode_attention(qf, idx, c.K_src, c.V_src, n, n, c.Krec, c.Vrec, self.max_new,
                                out_dtype=torch.bfloat16)
         return out.view(B, Hq, 1, D)

@@ -155,3 +155,32 @@ def test_qwen2_without_qk_norm(klt):
     finally:
         dec.free()
         dec.unpatch()
+
+
+@pytest.mark.parametrize("index,rows", [("host", "host"), ("hbm", "hbm")])
+def test_graph_decode_matches_eager(index, rows):
+    """graphs=True: eager steps until the local window lies in the recent buffer, then one captured
+    graph replayed per token.  Every step's logits equal the all-eager decoder's bit for bit."""
+    from fathom_b200.hf import OffloadedDecoder
+    model = _model()
+    B, n, steps = 2, 1500, 14
+    ids = torch.randint(0, 512, (B, n + steps), device="cuda", generator=torch.Generator("cuda").manual_seed(7))
+
+    def run(graphs):
+        dec = OffloadedDecoder(model, k=200, sink=4, local=8, index=index, rows=rows, max_new=16, graphs=graphs,
+                               prefill_chunk=512)
+        try:
+            dec.prefill(ids[:, :n])
+            dec.offload()
+            out = [dec.decode(ids[:, n + s:n + s + 1]) for s in range(steps)]
+            used = dec._graph is not None
+        finally:
+            dec.free()
+            dec.unpatch()
+        return out, used
+
+    eager, _ = run(False)
+    graph, used = run(True)
+    assert used
+    for s, (a, b) in enumerate(zip(eager, graph)):
+        assert torch.equal(a, b), s
