@@ -95,6 +95,7 @@ class OffloadedDecoder:
         self._scores = self._idx = self._arange_local = None
         self.graphs = graphs
         self._graph = self._graph_logits = None
+        self._graph_sig = None
         self._graph_mode = False
         self._ids_s = self._pos_s = self._slot_s = self._wbase_s = None
         for L, m in enumerate(self.attn):
@@ -279,7 +280,11 @@ class OffloadedDecoder:
         self._pos_s.fill_(c0.n + r)
         self._slot_s.fill_(r)
         self._wbase_s.fill_(c0.n + r + 1 - self.local)
+        sig = (self.k, tuple(self.budgets))          # baked into the capture: a change recaptures
+        if self._graph is not None and self._graph_sig != sig:
+            self._graph = self._graph_logits = None
         if self._graph is None:
+            self._graph_sig = sig
             self._graph_mode = True
             try:
                 with torch.no_grad():
