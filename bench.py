@@ -504,6 +504,59 @@ def klt_figure(a, bp, off, layers, kvs, n, BH, k_tot, scores):
             "extra_launches_per_layer": 1}
 
 
+def chan4_host_figure(a, dev, bp, off, layers, kv, scores):
+    """The reference's channel-subset comparators on the host-resident context of the headline step (its
+    offload-table rows SparQ r = 16 and the 32-channel scan, paper/tables/tab_offload.tex): per layer the
+    active channels (top-r of sum_g |q_g|, scripts/B_e2e_offload_v2.py:209), the zero-copy 4-bit scan of
+    the host channel store (HostChan4Store), sink+local top-k, and the same row gather + attention as
+    the bit-plane step.  4 distinct channel stores serve the layers round-robin (host memory); every
+    layer scans with its own query."""
+    from fathom_b200.synth import make_layer
+    n, BH = a.ctx, a.hkv
+    k_tot = a.k + a.sink + a.local
+    stores = []
+    for L in range(4):
+        d = make_layer(BH, a.g, n, seed=11, layer=L, device=dev, kv_dtype=torch.bfloat16, with_v=False)
+        stores.append(off.HostChan4Store(d["K"]))
+        del d
+    torch.cuda.empty_cache()
+    out = []
+    try:
+        for name, r in (("sparq_r16", 16), ("channels_32", 32)):
+            lists = []
+            for lay in layers:
+                m = torch.zeros(BH, 128, dtype=torch.bool, device=dev)
+                m.scatter_(1, lay.q.abs().sum(1).topk(r, -1).indices, True)
+                lists.append(m)
+
+            def step():
+                for L, lay in enumerate(layers):
+                    act, nact = bp.channel_list(lists[L])
+                    stores[L % len(stores)].scan(lay.q, act, nact, out=scores)
+                    idx = bp.sink_local_topk(scores, k_tot, a.sink, a.local)
+                    rows = kv[L % len(kv)]
+                    off.decode_attention(lay.q, idx, rows["K"], rows["V"], n)
+
+            for _ in range(a.warmup):
+                step()
+            torch.cuda.synchronize(dev)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for _ in range(a.steps):
+                step()
+            e1.record()
+            torch.cuda.synchronize(dev)
+            ms = e0.elapsed_time(e1) / a.steps
+            byts = bp.bytes_chan4(torch.full((BH,), r, dtype=torch.int32), n)
+            out.append({"method": name, "bits_per_row": byts * 8 / (n * BH), "ms_per_step": ms,
+                        "index_bytes_per_step": byts * len(layers),
+                        "index_gbs": byts * len(layers) / (ms * 1e-3) / 1e9})
+    finally:
+        for st in stores:
+            st.free()
+    return out
+
+
 def chan4_figure(a, bp, layers, peaks, n, BH, scores):
     """The reference's comparator scans on the same keys (kernels/bitplane.py Chan4Store; its kernel table
     rows): SparQ r = 16 (top-16 of sum_g |q_g|), 32 channels, and the full 4-bit scan, each a graph of scans
@@ -770,6 +823,7 @@ def main():
             "gpu_launches": launches_per_layer * a.layers * a.steps,
             "clocks": clk, "peaks_source": peaks_kind}
     if rank == 0 and world == 1 and not a.no_hbm and a.part == "all":
+        line["chan4_host"] = chan4_host_figure(a, dev, bp, off, layers, kv, scores)
         del layers, kv
         torch.cuda.empty_cache()
         line["hbm_resident"] = hbm_figure(a, dev, bp, off, peaks)

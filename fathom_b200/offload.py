@@ -130,6 +130,36 @@ class HostPlaneStore(bp.PlaneStore):
         self.scales_buf.free()
 
 
+class HostChan4Store(bp.Chan4Store):
+    """The comparator store (Chan4Store) in pinned, mapped host memory in the run order SUB = nblk: the
+    full 4-bit codes of one (bh, channel) are one contiguous run of nblk*32 bytes, the layout the
+    reference times its host-resident channel scans on (scripts/B_e2e_offload_v2.py:135-148, 290-296).
+    Built on the GPU, copied to the host; the device copies (and the codes) are released.  scan()
+    reads the listed channels' runs straight from host memory (zero-copy)."""
+
+    def __init__(self, K, scale_dtype=torch.float16, hugepages=False):
+        require_cuda(K)
+        old = bp.SUB
+        try:
+            bp.SUB = math.ceil(K.shape[1] / bp.BLK)
+            super().__init__(K, scale_dtype)
+        finally:
+            bp.SUB = old
+        self.chan_buf = MappedBuffer(self.chan_k.shape, torch.int32, K.device, hugepages)
+        self.scales_buf = MappedBuffer(self.scales_k.shape, torch.float16, K.device, hugepages)
+        self.chan_buf.dev.copy_(self.chan_k)
+        self.scales_buf.dev.copy_(self.scales_k)
+        torch.cuda.current_stream(K.device).synchronize()
+        self.chan_k = self.chan_buf.dev
+        self.scales_k = self.scales_buf.dev
+        self.code = None
+
+    def free(self):
+        self.chan_k = self.scales_k = None
+        self.chan_buf.free()
+        self.scales_buf.free()
+
+
 def gather_rows(src, cap, idx, BH, dtype=torch.bfloat16, D=128):
     """dst[bh, r, :] = src[bh, idx[bh, r], :] for bf16 rows; idx < 0 leaves the row zero; src may be a
     mapped host alias (scripts/B_e2e_offload_v2.py:73-83)."""

@@ -88,3 +88,28 @@ def test_chan4_orders_and_block_range():
     _store(bp, K, 16).scan(q, act, nact, out=out, blocks=(5, 11))
     assert torch.equal(out[..., 5 * 64:11 * 64], s16[..., 5 * 64:11 * 64])
     assert torch.all(out[..., :5 * 64] == 3.0) and torch.all(out[..., 11 * 64:] == 3.0)
+
+
+def test_host_chan4_store_matches_device_store():
+    """HostChan4Store (pinned mapped host memory, run order SUB = nblk, zero-copy scan) gives the same bits
+    as the device store in the same order."""
+    from fathom_b200 import bitplane as bp
+    from fathom_b200.offload import HostChan4Store
+    from fathom_b200.synth import make_layer
+    n = 20000
+    d = make_layer(2, 4, n, seed=9, kv_dtype=torch.bfloat16, with_v=False)
+    K, q = d["K"].cuda(), d["q"].cuda()
+    a = torch.zeros(2, 128, dtype=torch.bool, device="cuda")
+    a.scatter_(1, q.abs().sum(1).topk(16, -1).indices, True)
+    act, nact = bp.channel_list(a)
+    hs = HostChan4Store(K)
+    try:
+        assert hs.sub == math.ceil(n / 64) and hs.nsb == 1
+        s_host = hs.scan(q, act, nact)
+        s_dev = _store(bp, K, math.ceil(n / 64)).scan(q, act, nact)
+        assert torch.equal(s_host, s_dev)
+        code, sc = O.quantise_u4(d["K"].float().numpy())
+        ref = O.scan_chan4(d["q"].numpy(), code, sc, a.cpu().numpy())
+        assert score_rel_err(s_host.cpu().numpy(), ref) < 1e-5
+    finally:
+        hs.free()
