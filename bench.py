@@ -823,7 +823,10 @@ def main():
             "gpu_launches": launches_per_layer * a.layers * a.steps,
             "clocks": clk, "peaks_source": peaks_kind}
     if rank == 0 and world == 1 and not a.no_hbm and a.part == "all":
-        line["chan4_host"] = chan4_host_figure(a, dev, bp, off, layers, kv, scores)
+        try:
+            line["chan4_host"] = chan4_host_figure(a, dev, bp, off, layers, kv, scores)
+        except Exception as exc:                          # the headline line stands without this figure
+            line["chan4_host"] = {"error": f"{type(exc).__name__}: {str(exc)[:200]}"}
         del layers, kv
         torch.cuda.empty_cache()
         line["hbm_resident"] = hbm_figure(a, dev, bp, off, peaks)
