@@ -18,6 +18,8 @@ depends on the previous layer's output in a real model).
           this run (pinned H2D cudaMemcpy, 1 GiB)
   hbm_resident  config 1 (T = 131072, index + K/V in HBM) as a secondary figure, against
           MEASURED_PEAKS.json hbm_gbs (with the Chan4 comparator scans and the KLT-store step)
+  chan4_host  the reference's channel-subset comparators (SparQ r = 16, 32 channels) on the same
+          host-resident step, for the head-to-head of its offload table
   hf_decode  end to end through a Qwen3-8B-shaped transformers model (random weights) whose attention
           is patched onto this path, synthetic KV cache in host memory at 256k and 1M tokens: wall and
           CUDA-graph device ms per generated token (`--part hf` adds 512k)
