@@ -43,7 +43,9 @@ def test_patched_decode_with_full_k_is_dense_decode(index, rows, klt):
             o = model(ids[:, n + s:n + s + 1], past_key_values=past, use_cache=True)
             past = o.past_key_values
             ref.append(o.logits[:, -1])
-    dec = OffloadedDecoder(model, k=600, index=index, rows=rows, klt=klt, max_new=8, prefill_chunk=512)
+    # per-layer budgets (allocate_layer_budgets' output form): every layer plans on its own budget
+    dec = OffloadedDecoder(model, k=600, index=index, rows=rows, klt=klt, max_new=8, prefill_chunk=512,
+                           budget={0: 40, 1: 80})
     try:
         got_prefill = dec.prefill(ids[:, :n])
         assert _close(got_prefill, ref_prefill, 3e-2)
