@@ -38,6 +38,7 @@ import math
 import os
 import subprocess
 import sys
+import tempfile
 import time
 
 import numpy as np
@@ -88,12 +89,12 @@ class Clocks:
     def __init__(self, index):
         self.index = index
         self.proc = None
-        self.path = os.path.join(REPO, "gpurun_out", f"clocks_bench_{os.getpid()}.csv")
+        self.path = None
 
     def start(self):
         try:
-            os.makedirs(os.path.dirname(self.path), exist_ok=True)
-            self.f = open(self.path, "w")
+            fd, self.path = tempfile.mkstemp(prefix=f"fathom_clocks_{self.index}_", suffix=".csv")
+            self.f = os.fdopen(fd, "w")
             self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}",
                                           "--format=csv,noheader,nounits", "-lms", "200"], stdout=self.f,
                                          stderr=subprocess.DEVNULL)
@@ -111,10 +112,12 @@ class Clocks:
             self.proc.kill()
         self.f.close()
         rows = []
-        for line in open(self.path):
-            parts = [p.strip() for p in line.split(",")]
-            if len(parts) >= 8 and parts[1].replace(".", "").isdigit():
-                rows.append(parts)
+        with open(self.path) as f:
+            for line in f:
+                parts = [p.strip() for p in line.split(",")]
+                if len(parts) >= 8 and parts[1].replace(".", "").isdigit():
+                    rows.append(parts)
+        os.unlink(self.path)
         if not rows:
             return None
         sm = [float(r[1]) for r in rows]

@@ -35,6 +35,9 @@ SIGNATURES = {
     "fathom_pack_codes": (I32, [P, I64, I64, I64, P, P]),
     "fathom_unpack_planes": (I32, [P, I64, I64, I64, P, P]),
     "fathom_relayout": (I32, [P, P, I64, I64, I64, P, P, I64, P]),
+    "fathom_dequant_planes": (I32, [P, P, I32, I64, I64, P, I64, P, P]),
+    "fathom_scan_planes_reference": (I32, [P, I64, I32, I64, P, P, I32, P, P, P]),
+    "fathom_scan_chan4_reference": (I32, [P, I64, I32, I64, P, P, I32, P, P, P]),
     "fathom_make_plan": (I32, [P, P, I64, I32, I32, P, P, P, P, P, P, P, P]),
     "fathom_scan": (I32, [P, I64, I32, I64, I64, P, P, I32, P, P, I64, I64, P, P]),
     "fathom_wait_timeouts": (I32, [P, I32]),

@@ -105,6 +105,75 @@ def bytes_planes(t, n):
     return float(((t.float().sum(-1) * 8 + (t > 0).float().sum(-1) * 2) * nb).sum())
 
 
+# ------------------------------------------------------------------ dense reference helpers
+def _scales_arg(scales):
+    if scales.dtype == torch.float16:
+        return scales.contiguous(), 0
+    return scales.contiguous().float(), 1
+
+
+def dequant_planes(code, scales, t):
+    """Dequantisation of the top-t planes: code uint8 [..., n, D], scales [..., nblk, D] (fp16 or fp32),
+    t a depth (int), depths [D], or per-row depths [..., D] -> fp32 [..., n, D] with
+    ((c >> (4-t)) + 0.5 - 2^(t-1)) * s / 2^(t-1), 0 where t == 0 (kernels/bitplane.py:34-42)."""
+    require_cuda(code, scales)
+    *lead, n, d = code.shape
+    if d != D or code.dtype != torch.uint8:
+        raise ValueError("dequant_planes: codes must be uint8 [..., n, 128]")
+    rows = math.prod(lead) if lead else 1
+    sc, sf32 = _scales_arg(scales)
+    if tuple(sc.shape) != (*lead, _nblk(n), D):
+        raise ValueError(f"dequant_planes: scales must be [..., {_nblk(n)}, {D}]")
+    tt = torch.as_tensor(t, device=code.device).to(torch.int32)
+    if tt.dim() == 0:
+        tt = tt.expand(D)
+    if tt.dim() == 1:
+        stride = 0
+    elif tuple(tt.shape) == (*lead, D):
+        stride = D
+    else:
+        raise ValueError("dequant_planes: t must be a scalar, [128] or [..., 128] matching the codes")
+    tt = tt.contiguous()
+    out = torch.empty(*lead, n, D, dtype=torch.float32, device=code.device)
+    check(lib().fathom_dequant_planes(ptr(code.contiguous()), ptr(sc), sf32, rows, n, ptr(tt), stride, ptr(out),
+                                      stream_of(code.device)), "dequant_planes")
+    return out
+
+
+def _ref_scan_args(q, code, scales):
+    require_cuda(q, code, scales)
+    BH, G, d = q.shape
+    if d != D or code.dim() != 3 or code.shape[0] != BH or code.shape[2] != D or code.dtype != torch.uint8:
+        raise ValueError("scan reference: q [BH, G, 128] and codes uint8 [BH, n, 128] expected")
+    n = code.shape[1]
+    sc, sf32 = _scales_arg(scales)
+    if tuple(sc.shape) != (BH, _nblk(n), D):
+        raise ValueError(f"scan reference: scales must be [BH, {_nblk(n)}, {D}]")
+    out = torch.empty(BH, G, n, dtype=torch.float32, device=q.device)
+    return BH, G, n, q.contiguous().float(), code.contiguous(), sc, sf32, out
+
+
+def scan_planes_reference(q, code, scales, t):
+    """Dense scan of the plane semantics: q [BH, G, D] against dequant_planes(code[b], scales[b], t[b]) for
+    codes uint8 [BH, n, D], scales [BH, nblk, D] and depths t [BH, D] -> fp32 [BH, G, n]
+    (kernels/bitplane.py:357-363)."""
+    BH, G, n, qc, cc, sc, sf32, out = _ref_scan_args(q, code, scales)
+    tt = torch.as_tensor(t, device=q.device).to(torch.int32).expand(BH, D).contiguous()
+    check(lib().fathom_scan_planes_reference(ptr(qc), BH, G, n, ptr(cc), ptr(sc), sf32, ptr(tt), ptr(out),
+                                             stream_of(q.device)), "scan_planes_reference")
+    return out
+
+
+def scan_chan4_reference(q, code, scales, active):
+    """Dense scan of the comparator semantics: every channel at 4 bits times its active flag (active bool
+    [BH, D]) against q [BH, G, D] -> fp32 [BH, G, n] (kernels/bitplane.py:365-370)."""
+    BH, G, n, qc, cc, sc, sf32, out = _ref_scan_args(q, code, scales)
+    act = torch.as_tensor(active, device=q.device).to(torch.uint8).expand(BH, D).contiguous()
+    check(lib().fathom_scan_chan4_reference(ptr(qc), BH, G, n, ptr(cc), ptr(sc), sf32, ptr(act), ptr(out),
+                                            stream_of(q.device)), "scan_chan4_reference")
+    return out
+
+
 # ------------------------------------------------------------------ plan
 _BUDGETS = {}
 
@@ -147,6 +216,13 @@ def make_plan(g, budget, bmax=4, iters=30):
     check(lib().fathom_make_plan(ptr(gc), ptr(budget), BH, bmax, iters, ptr(t), ptr(pairs), ptr(npairs), ptr(act),
                                  ptr(nact), ptr(cls), ptr(clsn), stream_of(dev)), "make_plan")
     return {"t": t, "pairs": pairs, "npairs": npairs, "act": act, "nact": nact, "cls": cls, "clsn": clsn}
+
+
+def make_plan_torch(g, budget, bmax=4, iters=30):
+    """The water-filling depths alone, as float [BH, D] (kernels/bitplane.py:118-126): the same bisection
+    (lo = -60, hi = 60, `iters` halvings, round half to even, clip to 0..bmax) as make_plan, whose
+    depths it returns."""
+    return make_plan(g, budget, bmax, iters)["t"].float()
 
 
 # ------------------------------------------------------------------ store + scan

@@ -28,7 +28,6 @@
 //               and an index-ordered compaction of the keys equal to the threshold.
 #include "select_common.cuh"
 
-#include <atomic>
 
 namespace fathom {
 using namespace selectk;
@@ -837,9 +836,13 @@ extern "C" int fathom_merge_topk(const float* cand_scores, const int64_t* cand_i
 // that cannot accept cudaMalloc's implicit device synchronisation), and so cannot provide the
 // workspace fathom_sink_local_topk asks for.  The scratch is one file-scope device array sized for
 // FATHOM_STATIC_TOPK_MAX_ROWS rows; every GPU that loads this library holds it until the process
-// exits.  Every call on a device shares it: calls whose GPU work overlaps (other streams, other
-// host threads) race on it and must be serialised by the caller.  Each call clears the part that
-// has to start at zero (histograms and counters); the rest is overwritten before it is read.
+// exits.  The array is created when the CUDA module of this file is loaded on a device: with CUDA's
+// default lazy module loading that is the first call on that device which touches the module (this
+// entry point's address look-up, or any selection call), so such a call belongs before the host pools
+// its device memory or captures a stream.  Every call on a device shares the array: calls whose GPU
+// work overlaps (other streams, other host threads) race on it and must be serialised by the caller.
+// Each call clears the part that has to start at zero (histograms and counters); the rest is
+// overwritten before it is read.
 namespace fathom {
 namespace {
 
@@ -847,24 +850,15 @@ constexpr size_t kStaticScratchBytes = ws_bytes(FATHOM_STATIC_TOPK_MAX_ROWS);
 
 static __device__ __align__(256) unsigned char g_topk_scratch[kStaticScratchBytes];
 
-constexpr int kMaxDevices = 64;
-std::atomic<void*> g_topk_scratch_ptr[kMaxDevices];
-
 // Device address of g_topk_scratch on the current device.  In host code the array's name is only a
-// host-side stand-in, so the address is looked up once per device (with that device current) and
-// cached; the first call on each device therefore does this set-up.
+// host-side stand-in, so the address is looked up with the device current, on every call: once the
+// module is loaded the look-up is a table read, and a context torn down and created again (a device
+// reset) can never leave a stale address behind.
 int static_scratch(void** out) {
-  int dev = 0;
-  cudaError_t e = cudaGetDevice(&dev);
-  if (e != cudaSuccess) return set_error(FATHOM_ERR_CUDA, "sink_local_topk_static: cudaGetDevice: %s", cudaGetErrorString(e));
-  if (dev < 0 || dev >= kMaxDevices) return set_error(FATHOM_ERR_UNSUPPORTED, "sink_local_topk_static: device %d", dev);
-  void* p = g_topk_scratch_ptr[dev].load(std::memory_order_acquire);
-  if (p == nullptr) {
-    e = cudaGetSymbolAddress(&p, g_topk_scratch);
-    if (e != cudaSuccess || p == nullptr)
-      return set_error(FATHOM_ERR_CUDA, "sink_local_topk_static: cudaGetSymbolAddress: %s", cudaGetErrorString(e));
-    g_topk_scratch_ptr[dev].store(p, std::memory_order_release);
-  }
+  void* p = nullptr;
+  const cudaError_t e = cudaGetSymbolAddress(&p, g_topk_scratch);
+  if (e != cudaSuccess || p == nullptr)
+    return set_error(FATHOM_ERR_CUDA, "sink_local_topk_static: cudaGetSymbolAddress: %s", cudaGetErrorString(e));
   *out = p;
   return FATHOM_OK;
 }

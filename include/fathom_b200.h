@@ -76,6 +76,28 @@ int fathom_unpack_planes(const uint64_t* planes_k, int64_t BH, int64_t n, int64_
 int fathom_relayout(const uint64_t* planes_src, const uint16_t* scales_src, int64_t BH, int64_t nblk, int64_t sub_src,
                     uint64_t* planes_dst, uint16_t* scales_dst, int64_t sub_dst, void* stream);
 
+/* ---------------------------------------------------------------- dense reference helpers */
+
+/* dequant_planes (kernels/bitplane.py:34-42): out [rows][n][128] fp32 = the top-t planes of the
+ * codes dequantised, ((c >> (4-t)) + 0.5 - 2^(t-1)) * s / 2^(t-1) in that fp32 order, 0 where t = 0.
+ *   code [rows][n][128] uint8; scales [rows][ceil(n/64)][128] block absmax, fp32 if scales_f32 else fp16;
+ *   t int32 depths, [128] shared by every row (t_stride_row = 0) or [rows][128] (t_stride_row = 128);
+ *   depths above 4 are read as 4. */
+int fathom_dequant_planes(const uint8_t* code, const void* scales, int scales_f32, int64_t rows, int64_t n,
+                          const int32_t* t, int64_t t_stride_row, float* out, void* stream);
+
+/* scan_planes_reference (kernels/bitplane.py:357-363): scores [BH][G][n] = q [BH][G][128] times the
+ * dequant_planes values of code [BH][n][128] (16-byte aligned) with per-row depths t [BH][128] int32,
+ * summed over channels in ascending order.  G in 1..8. */
+int fathom_scan_planes_reference(const float* q, int64_t BH, int G, int64_t n, const uint8_t* code,
+                                 const void* scales, int scales_f32, const int32_t* t, float* scores, void* stream);
+
+/* scan_chan4_reference (kernels/bitplane.py:365-370): as fathom_scan_planes_reference with every
+ * channel at depth 4, each value multiplied by its channel's active flag (active [BH][128], 0/1 bytes). */
+int fathom_scan_chan4_reference(const float* q, int64_t BH, int G, int64_t n, const uint8_t* code,
+                                const void* scales, int scales_f32, const uint8_t* active, float* scores,
+                                void* stream);
+
 /* ---------------------------------------------------------------- plan */
 
 /* Per-(batch, kv-head) reverse water-filling plan (plan_kernel + make_plan,
@@ -196,10 +218,14 @@ int fathom_sink_local_topk(const float* scores, int64_t rows, int64_t n, int64_t
  * cudaMalloc's implicit device synchronisation).  No counterpart in the reference.
  * Scratch: one library-owned device array of about 5.3 MB, sized for FATHOM_STATIC_TOPK_MAX_ROWS
  * rows, held by every GPU that loads the library until the process exits.  rows above that limit
- * are rejected with FATHOM_ERR_SHAPE.  The first call on a device looks up the array's device
- * address (cudaGetSymbolAddress) with that device current; make that first call before any
- * stream capture.  All calls on a device share the array: calls whose GPU work overlaps
- * (different streams or threads) race on it, so serialise them. */
+ * are rejected with FATHOM_ERR_SHAPE.  The array comes into existence when the driver loads the
+ * library's selection module on a device; under CUDA's default lazy module loading that is the
+ * first call on the device that uses the module (this function, or any selection call), which is
+ * where its 5.3 MB are taken.  So make one such call on each device before handing the rest of
+ * its memory to a pool and before any stream capture (or run with CUDA_MODULE_LOADING=EAGER).
+ * Every call looks up the array's device address (cudaGetSymbolAddress) with the device current.
+ * All calls on a device share the array: calls whose GPU work overlaps (different streams or
+ * threads) race on it, so serialise them. */
 int fathom_sink_local_topk_static(const float* scores, int64_t rows, int64_t n, int64_t k, int64_t sink,
                                   int64_t local, int64_t* idx, void* stream);
 

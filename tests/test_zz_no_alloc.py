@@ -54,6 +54,44 @@ def test_static_scratch_topk_matches_workspace_variant_twice():
         assert torch.equal(got, ref)
 
 
+def test_static_scratch_histogram_path_after_group_path():
+    """The histogram path, whose counters must start at zero in the shared scratch, right after calls
+    that left the scratch dirty: a dense k (too few 32-token groups for the group-key path), and rows
+    whose group keys do not fit the scratch (64 x 1M), each compared with the workspace variant."""
+    L = _lib.lib()
+    torch.cuda.set_device(0)
+    g = torch.Generator(device="cuda").manual_seed(77)
+    warm = torch.randn(32, 131072, generator=g, device="cuda")
+    dense = torch.randn(64, 4096, generator=g, device="cuda")
+    big = torch.randn(64, 1 << 20, generator=g, device="cuda")
+    for s, k, sink, local in ((warm, 580, 4, 64), (dense, 1500, 4, 64), (warm, 580, 4, 64), (big, 580, 4, 64),
+                              (dense, 1500, 4, 64)):
+        got = _static(L, s, k, sink, local)
+        torch.cuda.synchronize()
+        ref = _with_workspace(L, s, k, sink, local)
+        torch.cuda.synchronize()
+        assert torch.equal(got, ref)
+
+
+def test_static_scratch_call_takes_no_device_memory():
+    """Once the library's selection module is loaded on the device (any earlier call), a call takes no
+    device memory: the free memory the driver reports is the same before and after it."""
+    L = _lib.lib()
+    torch.cuda.set_device(0)
+    g = torch.Generator(device="cuda").manual_seed(3)
+    s = torch.randn(64, 1 << 20, generator=g, device="cuda")
+    idx = torch.empty(64, 580, dtype=torch.int64, device="cuda")
+    st = torch.cuda.current_stream().cuda_stream
+    assert L.fathom_sink_local_topk_static(s.data_ptr(), 64, 1 << 20, 580, 4, 64, idx.data_ptr(), st) == 0
+    torch.cuda.synchronize()
+    free0, _ = torch.cuda.mem_get_info()
+    for _ in range(2):
+        assert L.fathom_sink_local_topk_static(s.data_ptr(), 64, 1 << 20, 580, 4, 64, idx.data_ptr(), st) == 0
+    torch.cuda.synchronize()
+    free1, _ = torch.cuda.mem_get_info()
+    assert free0 == free1
+
+
 def test_static_scratch_rejects_rows_beyond_its_limit():
     L = _lib.lib()
     p = ctypes.c_void_p(256)        # never dereferenced: the row check fails first
