@@ -140,7 +140,8 @@ __global__ void __launch_bounds__(WARPS * 32, (min_blocks<TPL, G>()))
   constexpr uint32_t ROW_BYTES = TILE_BLOCKS * 8;     // one (channel, plane) run of the tile
   constexpr uint32_t SROW_BYTES = TILE_BLOCKS * 2;    // one channel's scales of the tile
   extern __shared__ __align__(16) uint32_t s_stage[];  // [2][STAGE_U32]
-  __shared__ float s_q[G][D];
+  __shared__ float s_q2[G][D];                 // 2 q of channel j
+  __shared__ float s_qk[G][D];                 // q of channel j times 2^-t_j - 3
   __shared__ int s_ch[D], s_t[D], s_slot[D];
   __shared__ uint16_t s_pair[D * NPLANES];     // word position -> channel | plane << 8
   __shared__ int s_bstart[MAXB + 1], s_wstart[MAXB + 1];
@@ -149,9 +150,8 @@ __global__ void __launch_bounds__(WARPS * 32, (min_blocks<TPL, G>()))
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int64_t bh = blockIdx.y;
-  for (int e = tid; e < G * D; e += blockDim.x) s_q[e / D][e % D] = q[bh * G * D + e];
-  // one round of global loads: the query tile above, and here every thread's column of the four
-  // class lists plus the class counts; then the flat channel list in class order (depth 1, 2, 3, 4).
+  // one round of global loads: every thread's column of the four class lists plus the class counts;
+  // then the flat channel list in class order (depth 1, 2, 3, 4) and the per-channel head tables.
   // Entry i of class c sits at flat index cstart[c] + i and word position cword[c] + c * i; its batch
   // is position / WB; s_pair maps every word position to its (channel, plane).
   int cnt4[NPLANES];
@@ -215,6 +215,13 @@ __global__ void __launch_bounds__(WARPS * 32, (min_blocks<TPL, G>()))
         s_nb = b + 1;
         s_bstart[b + 1] = m + 1;
         s_wstart[b + 1] = slot + t;
+      }
+      const float KC = __uint_as_float(0x3F800000u - ((uint32_t)t << 23)) - 3.0f;   // 2^-t - 3
+#pragma unroll
+      for (int g = 0; g < G; ++g) {
+        const float qv = q[(bh * G + g) * D + ch];
+        s_q2[g][ch] = 2.0f * qv;
+        s_qk[g][ch] = qv * KC;
       }
     }
   }
@@ -352,12 +359,10 @@ __global__ void __launch_bounds__(WARPS * 32, (min_blocks<TPL, G>()))
 #pragma unroll
       for (int p = 0; p < 4; ++p) w[p] = (p < t && active) ? (wbuf[(slot + p) * TW + col] >> bitoff) : 0u;
       float W[G];
-      const float KC = __uint_as_float(0x3F800000u - ((uint32_t)t << 23)) - 3.0f;   // 2^-t - 3
 #pragma unroll
       for (int g = 0; g < G; ++g) {
-        const float qs = s_q[g][ch] * sc;
-        W[g] = 2.0f * qs;
-        cst[g] = fmaf(qs, KC, cst[g]);
+        W[g] = s_q2[g][ch] * sc;
+        cst[g] = fmaf(sc, s_qk[g][ch], cst[g]);
       }
       switch (t) {
         case 1: tokens<G, TPL, 1>(acc, w, W); break;
@@ -472,6 +477,8 @@ int launch_scan(const float* q, int64_t BH, int64_t n, int64_t nblk, int64_t nsb
 }  // namespace
 }  // namespace fathom
 
+#include "scan_phase.cuh"
+
 using namespace fathom;
 
 namespace fathom {
@@ -486,6 +493,65 @@ int sm_count() {
     cached[dev] = v > 0 ? v : 148;
   }
   return cached[dev];
+}
+
+// Resident CTAs of a kernel on the current device (cached per device and kernel).
+template <typename K>
+int resident_ctas(K kernel, int threads, size_t smem) {
+  static int cached[64] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) dev = 0;
+  if (cached[dev] == 0) {
+    int per_sm = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, threads, smem) != cudaSuccess || per_sm < 1)
+      per_sm = 1;
+    cached[dev] = per_sm * sm_count();
+  }
+  return cached[dev];
+}
+
+template <int G, int P, int FM>
+int launch_phase_scan(const float* q, int64_t BH, int64_t n, int64_t nblk, int64_t nsb, int64_t sub, const int32_t* cls,
+                      const int32_t* clsn, int bmax, const uint32_t* planes32, const uint16_t* scales, int64_t b0,
+                      int64_t b1, float* out, uint32_t* gkey, cudaStream_t st) {
+  using Ge = ph::Geo<P>;
+  const int64_t tile_lo = b0 / Ge::BPT, tile_hi = cdiv(b1, Ge::BPT);
+  const int64_t ntiles = tile_hi - tile_lo;
+  const size_t smem = (size_t)ph::WARPS * ph::NSTAGE * Ge::STAGE_U32 * sizeof(uint32_t);
+  auto kernel = ph::phase_scan_kernel<G, P, FM>;
+  cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  // tiles per warp: one while the grid fills fewer than ~4 waves of resident CTAs, more (up to 8) to
+  // spread each CTA's plan set-up over more tiles once it fills many waves
+  const int64_t ctas1 = BH * cdiv(ntiles, ph::WARPS);
+  const int64_t resident = resident_ctas(kernel, ph::WARPS * 32, smem);
+  int64_t tpw = ctas1 / (4 * resident);
+  tpw = tpw < 1 ? 1 : (tpw > 8 ? 8 : tpw);
+  if (const char* env = getenv("FATHOM_SCAN_TPW")) {    // tuning override
+    const int v = atoi(env);
+    if (v >= 1 && v <= 64) tpw = v;
+  }
+  const int64_t grid_x = cdiv(ntiles, ph::WARPS * tpw);
+  FATHOM_REQUIRE(grid_x <= 0x7fffffffLL && BH <= 65535, FATHOM_ERR_SHAPE, "scan: grid too large");
+  dim3 grid((unsigned)grid_x, (unsigned)BH);
+  kernel<<<grid, ph::WARPS * 32, smem, st>>>(q, cls, clsn, bmax, planes32, scales, n, nblk, nsb, sub, b0, b1, tile_lo,
+                                             tile_hi, out, gkey, selectk::n_groups(n));
+  return check_launch("scan");
+}
+
+// The phase-interleaved kernel takes stores in device memory whose superblock order keeps a warp tile
+// and its 8-block scale group inside one superblock row; mapped host memory keeps the bulk-copy
+// kernel, whose long runs suit the host link.
+bool phase_scan_applies(const uint64_t* planes_k, const uint16_t* scales_k, int64_t sub) {
+  if (const char* env = getenv("FATHOM_SCAN_KERNEL"))    // tuning override: "classic" keeps scan_kernel
+    if (!strcmp(env, "classic")) return false;
+  if (sub % 8 != 0 || (reinterpret_cast<uintptr_t>(planes_k) & 15) || (reinterpret_cast<uintptr_t>(scales_k) & 15))
+    return false;
+  cudaPointerAttributes a{};
+  if (cudaPointerGetAttributes(&a, planes_k) != cudaSuccess) {
+    cudaGetLastError();
+    return false;
+  }
+  return a.type == cudaMemoryTypeDevice || a.type == cudaMemoryTypeManaged;
 }
 
 int scan_dispatch(const float* q, int64_t BH, int G, int64_t n, int64_t sub, const int32_t* cls, const int32_t* clsn,
@@ -504,6 +570,40 @@ int scan_dispatch(const float* q, int64_t BH, int G, int64_t n, int64_t sub, con
                  (long long)nblk);
   if (blk_begin == blk_end) return FATHOM_OK;
   const uint32_t* p32 = reinterpret_cast<const uint32_t*>(planes_k);
+  if (phase_scan_applies(planes_k, scales_k, sub)) {
+    // two phases (16 tokens) per lane for G <= 4 unless that leaves the grid under one wave of warps
+    const int64_t range = blk_end - blk_begin;
+    const bool small = BH * cdiv(range, 8) * 2 < (int64_t)sm_count() * 32;
+    int P = (G <= 4 && !small) ? 2 : 1;
+    if (const char* env = getenv("FATHOM_SCAN_P")) {       // tuning override: 1 or 2 (2 only for G <= 4)
+      const int v = atoi(env);
+      if (v == 1 || (v == 2 && G <= 4)) P = v;
+    }
+    int FM = 1;
+    if (const char* env = getenv("FATHOM_SCAN_FM")) {      // tuning override: 0, 1 or 2
+      const int v = atoi(env);
+      if (v >= 0 && v <= 2) FM = v;
+    }
+#define FATHOM_PH3(GG, PP, FF) \
+  return launch_phase_scan<GG, PP, FF>(q, BH, n, nblk, nsb, sub, cls, clsn, bmax, p32, scales_k, blk_begin, blk_end, \
+                                       scores, gkey, st);
+#define FATHOM_PH(GG, PP) \
+  if (FM == 0) { FATHOM_PH3(GG, PP, 0) } \
+  if (FM == 2) { FATHOM_PH3(GG, PP, 2) } \
+  FATHOM_PH3(GG, PP, 1)
+    switch (G) {
+      case 1: if (P == 2) { FATHOM_PH(1, 2) } FATHOM_PH(1, 1)
+      case 2: if (P == 2) { FATHOM_PH(2, 2) } FATHOM_PH(2, 1)
+      case 3: if (P == 2) { FATHOM_PH(3, 2) } FATHOM_PH(3, 1)
+      case 4: if (P == 2) { FATHOM_PH(4, 2) } FATHOM_PH(4, 1)
+      case 5: FATHOM_PH(5, 1)
+      case 6: FATHOM_PH(6, 1)
+      case 7: FATHOM_PH(7, 1)
+      case 8: FATHOM_PH(8, 1)
+    }
+#undef FATHOM_PH
+#undef FATHOM_PH3
+  }
   // tokens per lane: 32 for G <= 4 (16 for G > 4, to bound registers); a split 4x finer only when the
   // coarse one would leave most SMs without a warp
   const int64_t range = blk_end - blk_begin;
