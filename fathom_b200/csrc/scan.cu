@@ -39,6 +39,8 @@
 #include <stdlib.h>
 #include <string.h>
 
+#include <mutex>
+
 namespace fathom {
 namespace {
 
@@ -495,19 +497,31 @@ int sm_count() {
   return cached[dev];
 }
 
-// Resident CTAs of a kernel on the current device (cached per device and kernel).
+// Resident CTAs of a kernel on the current device, cached per (device, kernel).
 template <typename K>
 int resident_ctas(K kernel, int threads, size_t smem) {
-  static int cached[64] = {0};
+  struct Entry {
+    const void* fn;
+    int dev;
+    int ctas;
+  };
+  static Entry cache[256];
+  static int used = 0;
+  static std::mutex mu;
+  std::lock_guard<std::mutex> lock(mu);
   int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) dev = 0;
-  if (cached[dev] == 0) {
-    int per_sm = 0;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, threads, smem) != cudaSuccess || per_sm < 1)
-      per_sm = 1;
-    cached[dev] = per_sm * sm_count();
+  if (cudaGetDevice(&dev) != cudaSuccess) dev = 0;
+  const void* fn = reinterpret_cast<const void*>(kernel);
+  for (int i = 0; i < used; ++i)
+    if (cache[i].fn == fn && cache[i].dev == dev) return cache[i].ctas;
+  int per_sm = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, threads, smem) != cudaSuccess || per_sm < 1) {
+    cudaGetLastError();
+    per_sm = 1;
   }
-  return cached[dev];
+  const int ctas = per_sm * sm_count();
+  if (used < 256) cache[used++] = Entry{fn, dev, ctas};
+  return ctas;
 }
 
 template <int G, int P, int FM>
@@ -518,7 +532,7 @@ int launch_phase_scan(const float* q, int64_t BH, int64_t n, int64_t nblk, int64
   const int64_t tile_lo = b0 / Ge::BPT, tile_hi = cdiv(b1, Ge::BPT);
   const int64_t ntiles = tile_hi - tile_lo;
   const size_t smem = (size_t)ph::WARPS * ph::NSTAGE * Ge::STAGE_U32 * sizeof(uint32_t);
-  auto kernel = ph::phase_scan_kernel<G, P, FM>;
+  auto kernel = gkey ? ph::phase_scan_kernel<G, P, FM, true> : ph::phase_scan_kernel<G, P, FM, false>;
   cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   // tiles per warp: one while the grid fills fewer than ~4 waves of resident CTAs, more (up to 8) to
   // spread each CTA's plan set-up over more tiles once it fills many waves

@@ -173,7 +173,7 @@ __device__ __forceinline__ void channel(Acc<G, P, FM>& acc, const uint32_t (&w)[
   }
 }
 
-template <int G, int P, int FM>
+template <int G, int P, int FM, bool GK>
 __global__ void __launch_bounds__(WARPS * 32, (P == 2 || G > 4 ? 3 : 4))
     phase_scan_kernel(const float* __restrict__ q, const int32_t* __restrict__ cls, const int32_t* __restrict__ clsn,
                       int bmax, const uint32_t* __restrict__ planes32, const uint16_t* __restrict__ scales, int64_t n,
@@ -324,6 +324,7 @@ __global__ void __launch_bounds__(WARPS * 32, (P == 2 || G > 4 ? 3 : 4))
     const int hi = (int)((hi_blk * BLK < n ? hi_blk * BLK : n) - tok0);
     float* s_sc = reinterpret_cast<float*>(st);
     const bool vec_ok = (n % 4 == 0) && ((reinterpret_cast<uintptr_t>(out) & 15) == 0);
+    const bool full = lo == 0 && hi == Ge::TILE_TOK;          // every token of the tile is written
     const int hwt = hw * 32;                                  // this lane's half-word, relative to the tile
 #pragma unroll
     for (int g = 0; g < G; ++g) {
@@ -335,9 +336,11 @@ __global__ void __launch_bounds__(WARPS * 32, (P == 2 || G > 4 ? 3 : 4))
         const float v = acc.get(g, k) + c;
         const int l = token_of<P>(k, r0);
         s_sc[hw * Ge::EPI_STRIDE + l] = v;
-        if (gkey && hwt + l >= lo && hwt + l < hi) gm = max(gm, f2key(v));
+        if constexpr (GK) {
+          if (full || (hwt + l >= lo && hwt + l < hi)) gm = max(gm, f2key(v));
+        }
       }
-      if (gkey) {
+      if constexpr (GK) {
 #pragma unroll
         for (int o = 1; o < Ge::LPH; o <<= 1) gm = max(gm, __shfl_xor_sync(0xffffffffu, gm, o));
         if (lane % Ge::LPH == 0 && hwt >= lo && hwt < hi) gkey[(bh * G + g) * ng + (tok0 + hwt) / 32] = gm;
@@ -348,7 +351,7 @@ __global__ void __launch_bounds__(WARPS * 32, (P == 2 || G > 4 ? 3 : 4))
       for (int it = 0; it < Ge::TILE_TOK / 128; ++it) {       // 128 tokens per warp instruction
         const int T = it * 128 + 4 * lane;
         const float4 v = *reinterpret_cast<const float4*>(s_sc + (T >> 5) * Ge::EPI_STRIDE + (T & 31));
-        if (vec_ok && T >= lo && T + 4 <= hi) {
+        if (vec_ok && (full || (T >= lo && T + 4 <= hi))) {
           *reinterpret_cast<float4*>(o + T) = v;
         } else {
           const float e[4] = {v.x, v.y, v.z, v.w};

@@ -87,6 +87,52 @@ def merge_shards(idx, vals, kk, merge_fn=None, gather_fn=None):
     return merge_fn(cv, ci, kk)
 
 
+def concurrent_probe(probe, rounds=5, group=None, sync=None):
+    """Runs probe() -> (bytes, seconds) on every rank at the same time, `rounds` times, each round started
+    by a barrier (and `sync`, e.g. a device synchronise).  Returns (aggregate, per_rank): the best
+    round's sum of bytes over its slowest rank's time, and each rank's own bytes / seconds in that
+    round.  All ranks take the same collective steps."""
+    import torch.distributed as dist
+    best = None
+    for _ in range(rounds):
+        if sync:
+            sync()
+        dist.barrier(group=group)
+        nbytes, sec = probe()
+        t = torch.tensor([float(nbytes), float(sec)], dtype=torch.float64)
+        allv = all_gather(t.to(_collective_device(group)), group).cpu()
+        agg = float(allv[:, 0].sum() / allv[:, 1].max())
+        if best is None or agg > best[0]:
+            best = (agg, [float(b / s) for b, s in allv.tolist()])
+    return best
+
+
+def _collective_device(group=None):
+    import torch.distributed as dist
+    if dist.get_backend(group) == "nccl":
+        return torch.device("cuda", torch.cuda.current_device())
+    return torch.device("cpu")
+
+
+def merged_equals_single(scores, top, n_total, kk, sink, local, select_fn=None, gather_fn=None):
+    """Checks a merged context-sharded selection against one selection over the whole context.
+
+    scores [BH, G, c] is this rank's chunk of the context's scores (equal chunks, rank order = context
+    order), top [BH, G, kk] the merged global indices.  The chunks are all-gathered into the full rows,
+    the top-kk of tokens [sink, n_total - local) is selected once, and the result is compared with `top`
+    (order included).  Per-token scores do not depend on the chunking (block-aligned chunks keep every
+    block's scale), so the full rows are exactly what a single-GPU scan of the context gives."""
+    if select_fn is None:
+        from .bitplane import select_topk
+        select_fn = lambda s, k, a, b: select_topk(s, k, mask_lo=a, mask_hi=b)
+    gather_fn = gather_fn or all_gather
+    parts = gather_fn(scores.contiguous())                  # [W, BH, G, c]
+    full = parts.permute(1, 2, 0, 3).reshape(scores.shape[0], scores.shape[1], -1)
+    assert full.shape[-1] == n_total, (full.shape, n_total)
+    single = select_fn(full, kk, sink, n_total - local)
+    return bool(torch.equal(single.to(top.device).to(torch.int64), top.to(torch.int64)))
+
+
 def sharded_decode_step(a, layers, kv, scores, outs, rank, world, q_in=None, g_in=None, scan_events=None):
     """One decode step over all layers on a context-sharded index (see the module docstring).
     `layers[L].store` holds this rank's chunk of a.ctx tokens; the context has a.ctx * world tokens."""

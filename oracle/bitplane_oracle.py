@@ -249,6 +249,26 @@ def scan_scores(q, code, scales, t):
     return out
 
 
+def scan_scores_threaded(q, code, scales, t, threads=None, chunk=1 << 15):
+    """scan_scores over token chunks on a thread pool (numpy releases the GIL in its array loops and the
+    BLAS product), so the restatement uses every host core as the reference's torch path does.  Chunks
+    are whole 64-token blocks; each chunk is scan_scores of its tokens and blocks."""
+    import os
+    from concurrent.futures import ThreadPoolExecutor
+    q = np.asarray(q, np.float32)
+    n = code.shape[-2]
+    chunk = max(BLK, chunk // BLK * BLK)
+    out = np.empty((q.shape[0], q.shape[1], n), np.float32)
+
+    def work(c0):
+        c1 = min(n, c0 + chunk)
+        out[..., c0:c1] = scan_scores(q, code[:, c0:c1], scales[:, c0 // BLK:nblocks(c1)], t)
+
+    with ThreadPoolExecutor(threads or os.cpu_count()) as ex:
+        list(ex.map(work, range(0, n, chunk)))
+    return out
+
+
 # ---------------------------------------------------------------- KLT-rotated store (planesK)
 def klt_basis(K, skip=16):
     """scripts/R_agent.py:59-63 (self_klt).  Keys [BH, n, D] after the first `skip` tokens (4 * SINK):

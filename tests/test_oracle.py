@@ -204,3 +204,15 @@ def test_layer_budget_allocation_matches_reference(a):
     err = {B: {L: float(E[i, L]) for L in range(E.shape[1])} for i, B in enumerate(budgets)}
     alloc = O.allocate_layer_budgets(err, budgets, float(z[f"{a}_target"]))
     assert [alloc[L] for L in range(E.shape[1])] == z[f"{a}_alloc"].tolist()
+
+
+def test_threaded_scan_equals_scan():
+    """The thread-pool scan the CPU baseline times computes the same scores as scan_scores."""
+    g = np.random.default_rng(7)
+    K = (g.standard_normal((2, 5000, 128)) * np.exp(g.standard_normal((2, 1, 128)))).astype(np.float32)
+    q = g.standard_normal((2, 4, 128)).astype(np.float32)
+    code, sc = O.quantise_u4(K)
+    t = g.integers(0, 5, (2, 128))
+    a = O.scan_scores(q, code, sc, t)
+    b = O.scan_scores_threaded(q, code, sc, t, threads=4, chunk=1000)
+    assert np.allclose(a, b, rtol=0, atol=1e-5 * np.abs(a).max())

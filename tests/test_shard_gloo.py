@@ -72,3 +72,48 @@ def test_chunk_bounds_and_windows():
     assert shard.local_window(0, 1000, 4000, 4, 64) == (4, 1000)
     assert shard.local_window(3000, 4000, 4000, 4, 64) == (0, 936)
     assert shard.local_window(3968, 4000, 4000, 4, 64) == (0, 0)
+
+
+def _oracle_single(s, kk, mask_lo, mask_hi):
+    m = s.numpy().copy()
+    m[..., :mask_lo] = -np.inf
+    m[..., mask_hi:] = -np.inf
+    return torch.from_numpy(O.topk_desc(m, kk))
+
+
+def _parity_rank(rank, world, port, scores, kk, sink, local, out):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    import datetime
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
+    try:
+        from fathom_b200 import shard
+        n = scores.shape[-1]
+        c = n // world
+        lo, hi = rank * c, (rank + 1) * c
+        top = shard.sharded_select(scores[..., lo:hi], kk, lo, hi, n, sink, local,
+                                   select_fn=_oracle_select, merge_fn=_oracle_merge)
+        good = shard.merged_equals_single(scores[..., lo:hi], top, n, kk, sink, local, select_fn=_oracle_single)
+        bad_top = top.clone()
+        bad_top[0, 0, [0, 1]] = bad_top[0, 0, [1, 0]]          # a merge that broke the order
+        bad = shard.merged_equals_single(scores[..., lo:hi], bad_top, n, kk, sink, local, select_fn=_oracle_single)
+        # concurrent probe: rank r moves (r + 1) GB in (r + 1) * 0.5 s -> aggregate 3 GB / 1 s
+        agg, per = shard.concurrent_probe(lambda: ((rank + 1) * 1e9, (rank + 1) * 0.5), rounds=2)
+        out[rank] = (good, bad, agg, per)
+    finally:
+        dist.destroy_process_group()
+
+
+def test_merged_parity_check_and_concurrent_probe_two_ranks():
+    """The bench's multi-GPU parity check (merged top-k vs one selection over the all-gathered score
+    chunks) accepts a correct merge and rejects a planted wrong one; the synchronised probe sums the
+    ranks' bytes over the slowest rank's time."""
+    g = torch.Generator().manual_seed(3)
+    scores = torch.randn(2, 3, 64 * 100, generator=g)
+    with mp.Manager() as mgr:
+        out = mgr.dict()
+        mp.spawn(_parity_rank, args=(2, _free_port(), scores, 300, 4, 64, out), nprocs=2, join=True)
+        for r in range(2):
+            good, bad, agg, per = out[r]
+            assert good and not bad
+            assert abs(agg - 3e9) < 1 and per == [2e9, 2e9]
