@@ -547,19 +547,24 @@ int launch_phase_scan(const float* q, int64_t BH, int64_t n, int64_t nblk, int64
   const int64_t grid_x = cdiv(ntiles, ph::WARPS * tpw);
   FATHOM_REQUIRE(grid_x <= 0x7fffffffLL && BH <= 65535, FATHOM_ERR_SHAPE, "scan: grid too large");
   dim3 grid((unsigned)grid_x, (unsigned)BH);
-  kernel<<<grid, ph::WARPS * 32, smem, st>>>(q, cls, clsn, bmax, planes32, scales, n, nblk, nsb, sub, b0, b1, tile_lo,
-                                             tile_hi, out, gkey, selectk::n_groups(n));
+  kernel<<<grid, ph::WARPS * 32, smem, st>>>(q, cls, clsn, bmax, planes32, scales, (int)n, (int)nsb, (int)sub, (int)b0,
+                                             (int)b1, (int)tile_lo, (int)tile_hi, out, gkey,
+                                             (int)selectk::n_groups(n));
   return check_launch("scan");
 }
 
 // The phase-interleaved kernel takes stores in device memory whose superblock order keeps a warp tile
 // and its 8-block scale group inside one superblock row; mapped host memory keeps the bulk-copy
 // kernel, whose long runs suit the host link.
-bool phase_scan_applies(const uint64_t* planes_k, const uint16_t* scales_k, int64_t sub) {
+bool phase_scan_applies(const uint64_t* planes_k, const uint16_t* scales_k, int64_t sub, int64_t nsb, int G,
+                        int64_t n) {
   if (const char* env = getenv("FATHOM_SCAN_KERNEL"))    // tuning override: "classic" keeps scan_kernel
     if (!strcmp(env, "classic")) return false;
   if (sub % 8 != 0 || (reinterpret_cast<uintptr_t>(planes_k) & 15) || (reinterpret_cast<uintptr_t>(scales_k) & 15))
     return false;
+  // the kernel's offsets within one row are 32-bit: the row's planes (1024 words per block) and its
+  // G score rows must stay below 2^31 elements
+  if (nsb * sub * 1024 >= (int64_t(1) << 31) || (int64_t)G * n >= (int64_t(1) << 31)) return false;
   cudaPointerAttributes a{};
   if (cudaPointerGetAttributes(&a, planes_k) != cudaSuccess) {
     cudaGetLastError();
@@ -584,7 +589,7 @@ int scan_dispatch(const float* q, int64_t BH, int G, int64_t n, int64_t sub, con
                  (long long)nblk);
   if (blk_begin == blk_end) return FATHOM_OK;
   const uint32_t* p32 = reinterpret_cast<const uint32_t*>(planes_k);
-  if (phase_scan_applies(planes_k, scales_k, sub)) {
+  if (phase_scan_applies(planes_k, scales_k, sub, nsb, G, n)) {
     // two phases (16 tokens) per lane for G <= 4 unless that leaves the grid under one wave of warps
     const int64_t range = blk_end - blk_begin;
     const bool small = BH * cdiv(range, 8) * 2 < (int64_t)sm_count() * 32;

@@ -174,11 +174,13 @@ __device__ __forceinline__ void channel(Acc<G, P, FM>& acc, const uint32_t (&w)[
 }
 
 template <int G, int P, int FM, bool GK>
-__global__ void __launch_bounds__(WARPS * 32, (P == 2 || G > 4 ? 3 : 4))
+__global__ void __launch_bounds__(WARPS * 32, (G > 4 ? 3 : 4))
     phase_scan_kernel(const float* __restrict__ q, const int32_t* __restrict__ cls, const int32_t* __restrict__ clsn,
-                      int bmax, const uint32_t* __restrict__ planes32, const uint16_t* __restrict__ scales, int64_t n,
-                      int64_t nblk, int64_t nsb, int64_t sub, int64_t blk_begin, int64_t blk_end, int64_t tile_lo,
-                      int64_t tile_hi, float* __restrict__ out, uint32_t* __restrict__ gkey, int64_t ng) {
+                      int bmax, const uint32_t* __restrict__ planes32, const uint16_t* __restrict__ scales, int n,
+                      int nsb, int sub, int blk_begin, int blk_end, int tile_lo, int tile_hi, float* __restrict__ out,
+                      uint32_t* __restrict__ gkey, int ng) {
+  // Offsets within one (batch, kv-head) row are 32-bit (the launcher keeps a row's store under 2^31
+  // words); the row's base pointers are formed once.
   using Ge = Geo<P>;
   constexpr int G2 = (G + 1) / 2;
   constexpr int TPL = Ge::TPL;
@@ -191,7 +193,7 @@ __global__ void __launch_bounds__(WARPS * 32, (P == 2 || G > 4 ? 3 : 4))
   __shared__ int s_nb, s_cstart[NPLANES + 1];
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int64_t bh = blockIdx.y;
+  const int bh = blockIdx.y;
   // ---- the row's channel list in class order, its copy batches and the per-entry head tables
   int cnt4[NPLANES], ch4[NPLANES];
 #pragma unroll
@@ -265,9 +267,9 @@ __global__ void __launch_bounds__(WARPS * 32, (P == 2 || G > 4 ? 3 : 4))
   const int nb = s_nb;
 
   // ---- this warp's tiles and lane geometry
-  const int64_t gw = (int64_t)blockIdx.x * WARPS + warp;
-  const int64_t wstride = (int64_t)gridDim.x * WARPS;
-  const int64_t ntw = tile_hi - tile_lo > gw ? (tile_hi - tile_lo - gw + wstride - 1) / wstride : 0;
+  const int gw = blockIdx.x * WARPS + warp;
+  const int wstride = gridDim.x * WARPS;
+  const int ntw = tile_hi - tile_lo > gw ? (tile_hi - tile_lo - gw + wstride - 1) / wstride : 0;
   if (ntw == 0) return;                                   // no barrier follows: warps are independent from here
   const int hw = lane / Ge::LPH;                          // half-word of the tile
   const int r0 = (lane % Ge::LPH) * P;                    // first phase of the lane
@@ -275,17 +277,19 @@ __global__ void __launch_bounds__(WARPS * 32, (P == 2 || G > 4 ? 3 : 4))
 #pragma unroll
   for (int k = 0; k < P + 3; ++k) amt[k] = (uint32_t)(6 - k - r0);
   uint32_t* my_stage = s_stage + (size_t)warp * NSTAGE * Ge::STAGE_U32;
-  const int64_t pstride32 = sub * 2;                      // 32-bit words between (channel, plane) rows
+  const int pstride32 = sub * 2;                          // 32-bit words between (channel, plane) rows
+  const uint32_t* planes_row = planes32 + (int64_t)bh * nsb * (D * NPLANES * 2) * sub;
+  const uint16_t* scales_row = scales + (int64_t)bh * nsb * D * sub;
   // items = (tile k of this warp, batch b) in order; 32-bit counters, advanced incrementally
-  const int items = (int)ntw * nb;
+  const int items = ntw * nb;
 
-  auto tile_of = [&](int k) { return tile_lo + gw + (int64_t)k * wstride; };
+  auto tile_of = [&](int k) { return tile_lo + gw + k * wstride; };
   // copies of item (k, b) into stage stg: 16-byte chunks, lane e of every 32
   auto issue = [&](int k, int b, int stg) {
-    const int64_t tb0 = tile_of(k) * Ge::BPT;
-    const int64_t sb = tb0 / sub, s_in = tb0 - sb * sub;
-    const uint32_t* rows = planes32 + ((bh * nsb + sb) * D * NPLANES * sub + s_in) * 2;
-    const uint16_t* srow = scales + (bh * nsb + sb) * D * sub + (s_in & ~(int64_t)7);
+    const int tb0 = tile_of(k) * Ge::BPT;
+    const int sb = tb0 / sub, s_in = tb0 - sb * sub;
+    const uint32_t* rows = planes_row + (sb * (D * NPLANES) * sub + s_in) * 2;
+    const uint16_t* srow = scales_row + sb * D * sub + (s_in & ~7);
     uint32_t* st = my_stage + stg * Ge::STAGE_U32;
     const int w0 = s_wstart[b], w1 = s_wstart[b + 1], c0 = s_bstart[b], c1 = s_bstart[b + 1];
     const int nrc = (w1 - w0) * Ge::CPR;
@@ -314,14 +318,14 @@ __global__ void __launch_bounds__(WARPS * 32, (P == 2 || G > 4 ? 3 : 4))
 
   // Epilogue of one tile: scores = acc + cst per head, staged in `st` (the stage just consumed) and
   // stored with 16-byte stores; group keys from the same floats.
-  auto epilogue = [&](int64_t tile, uint32_t* st) {
-    const int64_t tb0 = tile * Ge::BPT;
-    const int64_t tok0 = tb0 * BLK;                           // first token of the tile
-    const int64_t lo_blk = blk_begin > tb0 ? blk_begin : tb0;
-    const int64_t hi_blk = blk_end < tb0 + Ge::BPT ? blk_end : tb0 + Ge::BPT;
+  auto epilogue = [&](int tile, uint32_t* st) {
+    const int tb0 = tile * Ge::BPT;
+    const int tok0 = tb0 * BLK;                               // first token of the tile
+    const int lo_blk = blk_begin > tb0 ? blk_begin : tb0;
+    const int hi_blk = blk_end < tb0 + Ge::BPT ? blk_end : tb0 + Ge::BPT;
     // valid tokens of the tile, relative to its first token: [lo, hi)
-    const int lo = (int)((lo_blk - tb0) * BLK);
-    const int hi = (int)((hi_blk * BLK < n ? hi_blk * BLK : n) - tok0);
+    const int lo = (lo_blk - tb0) * BLK;
+    const int hi = (hi_blk * BLK < n ? hi_blk * BLK : n) - tok0;
     float* s_sc = reinterpret_cast<float*>(st);
     const bool vec_ok = (n % 4 == 0) && ((reinterpret_cast<uintptr_t>(out) & 15) == 0);
     const bool full = lo == 0 && hi == Ge::TILE_TOK;          // every token of the tile is written
@@ -343,10 +347,10 @@ __global__ void __launch_bounds__(WARPS * 32, (P == 2 || G > 4 ? 3 : 4))
       if constexpr (GK) {
 #pragma unroll
         for (int o = 1; o < Ge::LPH; o <<= 1) gm = max(gm, __shfl_xor_sync(0xffffffffu, gm, o));
-        if (lane % Ge::LPH == 0 && hwt >= lo && hwt < hi) gkey[(bh * G + g) * ng + (tok0 + hwt) / 32] = gm;
+        if (lane % Ge::LPH == 0 && hwt >= lo && hwt < hi) gkey[((int64_t)bh * G + g) * ng + (tok0 + hwt) / 32] = gm;
       }
       __syncwarp();
-      float* o = out + (bh * G + g) * n + tok0;
+      float* o = out + ((int64_t)bh * G + g) * n + tok0;
 #pragma unroll
       for (int it = 0; it < Ge::TILE_TOK / 128; ++it) {       // 128 tokens per warp instruction
         const int T = it * 128 + 4 * lane;
@@ -365,7 +369,7 @@ __global__ void __launch_bounds__(WARPS * 32, (P == 2 || G > 4 ? 3 : 4))
   };
 
   if (nb == 0) {                                              // no active channel: every score is 0
-    for (int kk = 0; kk < (int)ntw; ++kk) epilogue(tile_of(kk), my_stage);
+    for (int kk = 0; kk < ntw; ++kk) epilogue(tile_of(kk), my_stage);
     return;
   }
   const int sidx0 = hw >> 1;                                  // the lane's block within the tile
@@ -389,10 +393,10 @@ __global__ void __launch_bounds__(WARPS * 32, (P == 2 || G > 4 ? 3 : 4))
     issue_next();
     cp_async_wait<NSTAGE - 1>();                              // this lane's copies of item it have landed
     __syncwarp();                                             // ... and every lane's
-    const int64_t tile = tile_of(k);
+    const int tile = tile_of(k);
     const uint32_t* st = my_stage + sc * Ge::STAGE_U32;
     const uint16_t* srow16 = reinterpret_cast<const uint16_t*>(st + WBUF * Ge::HPW);
-    const int sidx = (int)((tile * Ge::BPT) & 7) + sidx0;    // block within the aligned 8-block scale group
+    const int sidx = ((tile * Ge::BPT) & 7) + sidx0;         // block within the aligned 8-block scale group
     const int c0 = s_bstart[b], c1 = s_bstart[b + 1];
 #pragma unroll
     for (int c = 0; c < NPLANES; ++c) {
