@@ -72,20 +72,20 @@ __device__ __forceinline__ void phase_words(const uint32_t (&w)[T], const uint32
   O = (__funnelshift_r(z, z, 4) & depth_mask(T)) | 0x80808080u;   // a rotation: token 28 + r wraps past bit 31
 }
 
+// Byte j of E / O moved to bits 16..23 of zero: the float f * 2^-126 (exponent field 1 from the byte's
+// 0x80, mantissa the code bits), exact.  Taking the other bytes from the zero register leaves the
+// permute without a constant operand.  The weights carry 2^63 (F_SCALE) and the epilogue multiplies the
+// sums by 2^63 (exact, power-of-two scaling while every product and sum stays normal), so the scores
+// are those of f itself.
 __device__ __forceinline__ uint32_t fbits(uint32_t X, int j) {
-  return __byte_perm(X, 0x3F000000u, 0x7044u | ((uint32_t)j << 8));
+  return __byte_perm(X, 0u, 0x4044u | ((uint32_t)j << 8));
 }
-// {f_a, f_b} built in one 64-bit register
+// {f_a, f_b} (scaled as above) built in one 64-bit register
 __device__ __forceinline__ float2 fpair(uint32_t Xa, uint32_t Xb, int j) {
-  unsigned long long r;
-  asm("{\n\t.reg .b32 lo, hi;\n\t"
-      "prmt.b32 lo, %1, %3, %4;\n\t"
-      "prmt.b32 hi, %2, %3, %4;\n\t"
-      "mov.b64 %0, {lo, hi};\n\t}"
-      : "=l"(r)
-      : "r"(Xa), "r"(Xb), "r"(0x3F000000u), "r"(0x7044u | ((uint32_t)j << 8)));
-  return *reinterpret_cast<float2*>(&r);
+  return make_float2(__uint_as_float(fbits(Xa, j)), __uint_as_float(fbits(Xb, j)));
 }
+constexpr float F_SCALE = 9223372036854775808.0f;   // 2^63: weights are 2q * 2^63
+constexpr float F_UNSCALE = 9223372036854775808.0f; // sums times 2^63 restore f's scale (2^-126 * 2^63 * 2^63)
 
 // Accumulators of one lane: TPL tokens x G heads in the layout of the FMA mode.
 template <int G, int P, int FM>
@@ -257,7 +257,7 @@ __global__ void __launch_bounds__(WARPS * 32, (G > 4 ? 3 : 4))
       for (int g = 0; g < G; ++g) qv[g] = q[(bh * G + g) * D + ch];
 #pragma unroll
       for (int k = 0; k < G2; ++k) {
-        const float a = 2.0f * qv[2 * k], b2 = 2 * k + 1 < G ? 2.0f * qv[2 * k + 1] : 0.0f;
+        const float a = 2.0f * qv[2 * k] * F_SCALE, b2 = 2 * k + 1 < G ? 2.0f * qv[2 * k + 1] * F_SCALE : 0.0f;
         s_qq[m][k] = make_float4(a, a, b2, b2);
         s_qk[m][k] = make_float2(qv[2 * k] * KC, 2 * k + 1 < G ? qv[2 * k + 1] * KC : 0.0f);
       }
@@ -337,7 +337,7 @@ __global__ void __launch_bounds__(WARPS * 32, (G > 4 ? 3 : 4))
       __syncwarp();
 #pragma unroll
       for (int k = 0; k < TPL; ++k) {
-        const float v = acc.get(g, k) + c;
+        const float v = fmaf(acc.get(g, k), F_UNSCALE, c);   // = (sum of W f) + cst, one rounding
         const int l = token_of<P>(k, r0);
         s_sc[hw * Ge::EPI_STRIDE + l] = v;
         if constexpr (GK) {
