@@ -524,7 +524,7 @@ int resident_ctas(K kernel, int threads, size_t smem) {
   return ctas;
 }
 
-template <int G, int P, int FM>
+template <int G, int P>
 int launch_phase_scan(const float* q, int64_t BH, int64_t n, int64_t nblk, int64_t nsb, int64_t sub, const int32_t* cls,
                       const int32_t* clsn, int bmax, const uint32_t* planes32, const uint16_t* scales, int64_t b0,
                       int64_t b1, float* out, uint32_t* gkey, cudaStream_t st) {
@@ -532,7 +532,7 @@ int launch_phase_scan(const float* q, int64_t BH, int64_t n, int64_t nblk, int64
   const int64_t tile_lo = b0 / Ge::BPT, tile_hi = cdiv(b1, Ge::BPT);
   const int64_t ntiles = tile_hi - tile_lo;
   const size_t smem = (size_t)ph::WARPS * ph::NSTAGE * Ge::STAGE_U32 * sizeof(uint32_t);
-  auto kernel = gkey ? ph::phase_scan_kernel<G, P, FM, true> : ph::phase_scan_kernel<G, P, FM, false>;
+  auto kernel = gkey ? ph::phase_scan_kernel<G, P, true> : ph::phase_scan_kernel<G, P, false>;
   cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   // tiles per warp: one while the grid fills fewer than ~4 waves of resident CTAs, more (up to 8) to
   // spread each CTA's plan set-up over more tiles once it fills many waves
@@ -598,18 +598,9 @@ int scan_dispatch(const float* q, int64_t BH, int G, int64_t n, int64_t sub, con
       const int v = atoi(env);
       if (v == 1 || (v == 2 && G <= 4)) P = v;
     }
-    int FM = 1;
-    if (const char* env = getenv("FATHOM_SCAN_FM")) {      // tuning override: 0, 1 or 2
-      const int v = atoi(env);
-      if (v >= 0 && v <= 2) FM = v;
-    }
-#define FATHOM_PH3(GG, PP, FF) \
-  return launch_phase_scan<GG, PP, FF>(q, BH, n, nblk, nsb, sub, cls, clsn, bmax, p32, scales_k, blk_begin, blk_end, \
-                                       scores, gkey, st);
 #define FATHOM_PH(GG, PP) \
-  if (FM == 0) { FATHOM_PH3(GG, PP, 0) } \
-  if (FM == 2) { FATHOM_PH3(GG, PP, 2) } \
-  FATHOM_PH3(GG, PP, 1)
+  return launch_phase_scan<GG, PP>(q, BH, n, nblk, nsb, sub, cls, clsn, bmax, p32, scales_k, blk_begin, blk_end, scores, \
+                                   gkey, st);
     switch (G) {
       case 1: if (P == 2) { FATHOM_PH(1, 2) } FATHOM_PH(1, 1)
       case 2: if (P == 2) { FATHOM_PH(2, 2) } FATHOM_PH(2, 1)
@@ -621,7 +612,6 @@ int scan_dispatch(const float* q, int64_t BH, int G, int64_t n, int64_t sub, con
       case 8: FATHOM_PH(8, 1)
     }
 #undef FATHOM_PH
-#undef FATHOM_PH3
   }
   // tokens per lane: 32 for G <= 4 (16 for G > 4, to bound registers); a split 4x finer only when the
   // coarse one would leave most SMs without a warp

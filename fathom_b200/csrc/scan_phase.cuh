@@ -15,10 +15,10 @@
 // float 1 + c_t / 2^t.  Per phase word that is 2t + 2 logic ops plus one prmt per token, against 2t
 // ops per token when f is assembled token by token.
 //
-// FMAs (FM): 0 = two tokens of a lane in a register pair, one fma.rn.f32x2 per head with W_g
-// duplicated; 1 = two query heads in a register pair (accumulators {acc_g, acc_g+1} of a token) and
-// f duplicated, one fma.rn.f32x2 per head pair; 2 = one fma.rn per head and token.  The halves of
-// fma.rn.f32x2 are independent fma.rn operations, so every mode gives the same sums.
+// Paired FMAs.  The accumulators of two query heads for one token share a 64-bit register pair
+// {acc_g, acc_g+1} and take one fma.rn.f32x2 with {W_g, W_g+1} and f duplicated; the halves are
+// independent fma.rn operations, so the sums are those of scan_kernel.  (Measured on config 1: pairing
+// two tokens per register with W duplicated, or scalar fma.rn, was 4% and 12% slower.)
 //
 // Work split.  A lane owns P phases (P = 2: 16 tokens; P = 1: 8 tokens) of one half-word; a warp
 // tile is 4P blocks of one (batch, kv-head) row.  Warps run independently: each streams its tiles'
@@ -80,36 +80,23 @@ __device__ __forceinline__ void phase_words(const uint32_t (&w)[T], const uint32
 __device__ __forceinline__ uint32_t fbits(uint32_t X, int j) {
   return __byte_perm(X, 0u, 0x4044u | ((uint32_t)j << 8));
 }
-// {f_a, f_b} (scaled as above) built in one 64-bit register
-__device__ __forceinline__ float2 fpair(uint32_t Xa, uint32_t Xb, int j) {
-  return make_float2(__uint_as_float(fbits(Xa, j)), __uint_as_float(fbits(Xb, j)));
-}
 constexpr float F_SCALE = 9223372036854775808.0f;   // 2^63: weights are 2q * 2^63
 constexpr float F_UNSCALE = 9223372036854775808.0f; // sums times 2^63 restore f's scale (2^-126 * 2^63 * 2^63)
 
-// Accumulators of one lane: TPL tokens x G heads in the layout of the FMA mode.
-template <int G, int P, int FM>
+// Accumulators of one lane: TPL tokens x G heads; pair k2 * TPL + slot holds heads 2k2, 2k2 + 1 of a token.
+template <int G, int P>
 struct Acc {
   static constexpr int TPL = 8 * P;
   static constexpr int G2 = (G + 1) / 2;
-  static constexpr int NR = FM == 0 ? G * (TPL / 2) : FM == 1 ? G2 * TPL : G * TPL / 2;
-  float2 r[NR];
+  float2 r[G2 * TPL];
   __device__ __forceinline__ void zero() {
 #pragma unroll
-    for (int i = 0; i < NR; ++i) r[i] = make_float2(0.f, 0.f);
+    for (int i = 0; i < G2 * TPL; ++i) r[i] = make_float2(0.f, 0.f);
   }
   // value of head g, lane token slot k (k = 2 * pair + half, see token_of)
   __device__ __forceinline__ float get(int g, int k) const {
-    if constexpr (FM == 0) {
-      const float2 v = r[g * (TPL / 2) + (k >> 1)];
-      return (k & 1) ? v.y : v.x;
-    } else if constexpr (FM == 1) {
-      const float2 v = r[(g >> 1) * TPL + k];
-      return (g & 1) ? v.y : v.x;
-    } else {
-      const float2 v = r[(g * TPL + k) >> 1];
-      return ((g * TPL + k) & 1) ? v.y : v.x;
-    }
+    const float2 v = r[(g >> 1) * TPL + k];
+    return (g & 1) ? v.y : v.x;
   }
 };
 
@@ -120,17 +107,10 @@ __device__ __forceinline__ int token_of(int k, int r0) {
   else return 4 * (k >> 1) + r0 + (k & 1);                         // phases r0, r0 + 1 of nibble m = k >> 1
 }
 
-// Weights of one channel in the layout of the FMA mode.
-template <int G, int FM>
-struct Wt {
-  static constexpr int G2 = (G + 1) / 2;
-  float2 w[FM == 1 ? G2 : G];
-};
-
-// One channel of depth T for one lane: P phase words, then TPL tokens x G heads.
-template <int T, int P, int G, int FM>
-__device__ __forceinline__ void channel(Acc<G, P, FM>& acc, const uint32_t (&w)[T], const uint32_t (&amt)[P + 3],
-                                        const Wt<G, FM>& W) {
+// One channel of depth T for one lane: P phase words, then TPL tokens x G2 head pairs.
+template <int T, int P, int G>
+__device__ __forceinline__ void channel(Acc<G, P>& acc, const uint32_t (&w)[T], const uint32_t (&amt)[P + 3],
+                                        const float2 (&W)[(G + 1) / 2]) {
   constexpr int TPL = 8 * P, G2 = (G + 1) / 2;
   uint32_t X[2][2];   // [phase][E, O]
   phase_words<T, 0>(w, amt, X[0][0], X[0][1]);
@@ -150,31 +130,18 @@ __device__ __forceinline__ void channel(Acc<G, P, FM>& acc, const uint32_t (&w)[
       xb = X[1][pr & 1];
       j = pr >> 1;
     }
-    if constexpr (FM == 0) {
-      const float2 f = fpair(xa, xb, j);
+    const float fa = __uint_as_float(fbits(xa, j)), fb = __uint_as_float(fbits(xb, j));
+    const float2 fa2 = make_float2(fa, fa), fb2 = make_float2(fb, fb);
 #pragma unroll
-      for (int g = 0; g < G; ++g) acc.r[g * (TPL / 2) + pr] = __ffma2_rn(W.w[g], f, acc.r[g * (TPL / 2) + pr]);
-    } else if constexpr (FM == 1) {
-      const float2 fa = fpair(xa, xa, j), fb = fpair(xb, xb, j);
-#pragma unroll
-      for (int k = 0; k < G2; ++k) {
-        acc.r[k * TPL + 2 * pr] = __ffma2_rn(W.w[k], fa, acc.r[k * TPL + 2 * pr]);
-        acc.r[k * TPL + 2 * pr + 1] = __ffma2_rn(W.w[k], fb, acc.r[k * TPL + 2 * pr + 1]);
-      }
-    } else {
-      const float fa = __uint_as_float(fbits(xa, j)), fb = __uint_as_float(fbits(xb, j));
-#pragma unroll
-      for (int g = 0; g < G; ++g) {
-        float2& v = acc.r[(g * TPL + 2 * pr) >> 1];   // TPL even: slots 2pr, 2pr + 1 share a pair
-        v.x = fmaf(W.w[g].x, fa, v.x);
-        v.y = fmaf(W.w[g].x, fb, v.y);
-      }
+    for (int k = 0; k < G2; ++k) {
+      acc.r[k * TPL + 2 * pr] = __ffma2_rn(W[k], fa2, acc.r[k * TPL + 2 * pr]);
+      acc.r[k * TPL + 2 * pr + 1] = __ffma2_rn(W[k], fb2, acc.r[k * TPL + 2 * pr + 1]);
     }
   }
 }
 
-template <int G, int P, int FM, bool GK>
-__global__ void __launch_bounds__(WARPS * 32, (G > 4 ? 3 : 4))
+template <int G, int P, bool GK>
+__global__ void __launch_bounds__(WARPS * 32, 4)
     phase_scan_kernel(const float* __restrict__ q, const int32_t* __restrict__ cls, const int32_t* __restrict__ clsn,
                       int bmax, const uint32_t* __restrict__ planes32, const uint16_t* __restrict__ scales, int n,
                       int nsb, int sub, int blk_begin, int blk_end, int tile_lo, int tile_hi, float* __restrict__ out,
@@ -185,8 +152,7 @@ __global__ void __launch_bounds__(WARPS * 32, (G > 4 ? 3 : 4))
   constexpr int G2 = (G + 1) / 2;
   constexpr int TPL = Ge::TPL;
   extern __shared__ __align__(16) uint32_t s_stage[];   // [WARPS][NSTAGE][STAGE_U32]
-  __shared__ float4 s_qq[D][G2];                        // flat entry i: {2q_g, 2q_g, 2q_g+1, 2q_g+1}, g = 2k
-  __shared__ float2 s_qk[D][G2];                        // flat entry i: {q_g * KC_t, q_g+1 * KC_t}
+  __shared__ float4 s_qt[D][G2];                        // flat entry i, g = 2k: {2q_g S, 2q_g+1 S, q_g KC_t, q_g+1 KC_t}
   __shared__ int s_ch[D], s_slot[D];
   __shared__ uint16_t s_pair[D * NPLANES];
   __shared__ int s_bstart[MAXB + 1], s_wstart[MAXB + 1];
@@ -258,8 +224,7 @@ __global__ void __launch_bounds__(WARPS * 32, (G > 4 ? 3 : 4))
 #pragma unroll
       for (int k = 0; k < G2; ++k) {
         const float a = 2.0f * qv[2 * k] * F_SCALE, b2 = 2 * k + 1 < G ? 2.0f * qv[2 * k + 1] * F_SCALE : 0.0f;
-        s_qq[m][k] = make_float4(a, a, b2, b2);
-        s_qk[m][k] = make_float2(qv[2 * k] * KC, 2 * k + 1 < G ? qv[2 * k + 1] * KC : 0.0f);
+        s_qt[m][k] = make_float4(a, b2, qv[2 * k] * KC, 2 * k + 1 < G ? qv[2 * k + 1] * KC : 0.0f);
       }
     }
   }
@@ -307,7 +272,7 @@ __global__ void __launch_bounds__(WARPS * 32, (G > 4 ? 3 : 4))
     }
   };
 
-  Acc<G, P, FM> acc;
+  Acc<G, P> acc;
   float2 cst[G2];
   auto reset = [&]() {
     acc.zero();
@@ -406,32 +371,26 @@ __global__ void __launch_bounds__(WARPS * 32, (G > 4 ? 3 : 4))
       for (int i = i0; i < i1; ++i) {
         const float s = __half2float(__ushort_as_half(srow16[(i - c0) * (Ge::SROW_U32 * 2) + sidx]));
         const float2 ss = make_float2(s, s);
-        Wt<G, FM> W;
+        float2 W[G2];
 #pragma unroll
         for (int k2 = 0; k2 < G2; ++k2) {
-          const float4 v = s_qq[i][k2];
-          if constexpr (FM == 1) {
-            W.w[k2] = __fmul2_rn(make_float2(v.x, v.z), ss);
-          } else {
-            W.w[2 * k2] = __fmul2_rn(make_float2(v.x, v.y), ss);
-            if (2 * k2 + 1 < G) W.w[2 * k2 + 1] = __fmul2_rn(make_float2(v.z, v.w), ss);
-          }
+          const float4 v = s_qt[i][k2];
+          W[k2] = __fmul2_rn(make_float2(v.x, v.y), ss);
+          cst[k2] = __ffma2_rn(ss, make_float2(v.z, v.w), cst[k2]);
         }
-#pragma unroll
-        for (int kk = 0; kk < G2; ++kk) cst[kk] = __ffma2_rn(ss, s_qk[i][kk], cst[kk]);
         const uint32_t* wr = st + s_slot[i] * Ge::HPW + hw;
         if (c == 0) {
           uint32_t w[1] = {wr[0]};
-          channel<1, P, G, FM>(acc, w, amt, W);
+          channel<1, P, G>(acc, w, amt, W);
         } else if (c == 1) {
           uint32_t w[2] = {wr[0], wr[Ge::HPW]};
-          channel<2, P, G, FM>(acc, w, amt, W);
+          channel<2, P, G>(acc, w, amt, W);
         } else if (c == 2) {
           uint32_t w[3] = {wr[0], wr[Ge::HPW], wr[2 * Ge::HPW]};
-          channel<3, P, G, FM>(acc, w, amt, W);
+          channel<3, P, G>(acc, w, amt, W);
         } else {
           uint32_t w[4] = {wr[0], wr[Ge::HPW], wr[2 * Ge::HPW], wr[3 * Ge::HPW]};
-          channel<4, P, G, FM>(acc, w, amt, W);
+          channel<4, P, G>(acc, w, amt, W);
         }
       }
     }
