@@ -465,12 +465,14 @@ def hbm_figure(a, dev, bp, off, peaks, spec="config1", batch=None, seed=None):
     f1.record()
     torch.cuda.synchronize()
     scan_ms = f0.elapsed_time(f1) / (a.steps * len(layers))
+    del gs
+    batched = batched_scan_figure(a, bp, layers, n, BH, G, peaks)
     byts = [lay.bytes for lay in layers]
     comparators = chan4_figure(a, bp, layers, peaks, n, BH, scores) if spec == "config1" else None
     klt_step = klt_figure(a, bp, off, layers, kvs, n, BH, k_tot, scores) if spec == "config1" else None
     achieved = float(np.mean(byts)) / (scan_ms * 1e-3) / 1e9
     rows = n * BH * nl
-    del gs, layers, kvs
+    del layers, kvs
     torch.cuda.empty_cache()
     return {"workload": sp["workload"],
             "value": rows / (ms * 1e-3), "unit": "key-rows/s", "ms_per_step": ms,
@@ -482,9 +484,58 @@ def hbm_figure(a, dev, bp, off, peaks, spec="config1", batch=None, seed=None):
                                            if spec == "config1" else "not captured",
                          "bytes_per_launch": float(np.mean(byts))},
             "bits_per_row": float(np.mean(byts)) * 8 / (n * BH),
+            "batched_scan": batched,
             **({"budget_sweep": sweep} if sweep else {}),
             **({"chan4_comparators": comparators} if comparators else {}),
             **({"klt_step": klt_step} if klt_step else {})}
+
+
+class _RowsStore:
+    """All layers' stores as one row set (layer-major rows), for one scan launch over every layer."""
+
+    def __init__(self, stores):
+        self.BH = sum(st.BH for st in stores)
+        self.n = stores[0].n
+        self.sub = stores[0].sub
+        self.planes_k = torch.cat([st.planes_k for st in stores])
+        self.planes32 = self.planes_k.view(torch.int32)
+        self.scales_k = torch.cat([st.scales_k for st in stores])
+
+
+def batched_scan_figure(a, bp, layers, n, BH, G, peaks):
+    """The scan of every layer's rows in ONE launch (layer-major rows; the queries of the synthetic
+    layers are independent): the kernel's throughput with enough rows to fill the machine, beside the
+    per-layer launches of the decode step.  Mean per layer-equivalent over a graph of launches; inputs
+    (the index of all layers, hundreds of MB) are larger than L2."""
+    rs = _RowsStore([lay.store for lay in layers])
+    q = torch.cat([lay.q for lay in layers])
+    plan = bp.make_plan(torch.cat([lay.g for lay in layers]), a.budget)
+    byts = bp.bytes_planes(plan["t"], n)
+    out = torch.empty(rs.BH, G, n, device=q.device)
+    reps = max(2, a.steps // 2)
+    for _ in range(3):
+        bp.PlaneStore.scan(rs, q, plan, out=out)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        for _ in range(reps):
+            bp.PlaneStore.scan(rs, q, plan, out=out)
+    g.replay()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    g.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / reps
+    nl = len(layers)
+    achieved = byts / (ms * 1e-3) / 1e9
+    del g, out, rs
+    torch.cuda.empty_cache()
+    return {"layers_per_launch": nl, "rows_per_launch": BH * nl, "us_per_layer": ms * 1e3 / nl,
+            "launch_ms": ms, "bytes_per_launch": byts,
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                         "frac": achieved / peaks["hbm_gbs"]}}
 
 
 def klt_figure(a, bp, off, layers, kvs, n, BH, k_tot, scores):
