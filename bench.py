@@ -71,8 +71,11 @@ def parse():
     ap.add_argument("--no-hf", action="store_true", help="skip the end-to-end transformers-model figure")
     ap.add_argument("--hf-ctx", default="", help="--part hf: comma-separated context lengths (default 256k, 512k, 1M)")
     ap.add_argument("--cpu-heads", type=int, default=2, help="KV heads of one layer in the CPU sample")
-    ap.add_argument("--part", choices=["all", "host", "hbm", "config3", "hf"], default="all",
-                    help="profiling runs: only the host-resident step (host) or only the HBM-resident figure (hbm)")
+    ap.add_argument("--part", choices=["all", "host", "hbm", "config3", "hf", "scan"], default="all",
+                    help="profiling runs: only the host-resident step (host), only the HBM-resident figure (hbm), "
+                         "or scan launches alone over --scan-layers layers of --scan-spec (scan)")
+    ap.add_argument("--scan-spec", choices=["config1", "config3"], default="config1")
+    ap.add_argument("--scan-layers", type=int, default=36, help="--part scan: layers whose rows one launch covers")
     return ap.parse_args()
 
 
@@ -538,6 +541,41 @@ def batched_scan_figure(a, bp, layers, n, BH, G, peaks):
                          "frac": achieved / peaks["hbm_gbs"]}}
 
 
+def scan_part(a, dev, bp, peaks):
+    """--part scan (profiling): one HBM store over --scan-layers layers of the --scan-spec shape (rows
+    layer-major, seeded lognormal-channel keys), 3 warm-up scans, then --steps timed scan launches over
+    all rows.  An ncu capture of one launch (`-k regex:phase_scan -s 2 -c 1`) sees a launch over every
+    layer's rows."""
+    sp = HBM_SPECS[a.scan_spec]
+    rows, G, n = sp["hkv"] * sp["batch"] * a.scan_layers, sp["g"], sp["n"]
+    gen = torch.Generator(device=dev).manual_seed(5)
+    scale = torch.randn(rows, 1, 128, generator=gen, device=dev).exp()
+    K = torch.empty(rows, n, 128, dtype=torch.bfloat16, device=dev)
+    for r0 in range(0, rows, 16):
+        r1 = min(rows, r0 + 16)
+        K[r0:r1] = (torch.randn(r1 - r0, n, 128, generator=gen, device=dev) * scale[r0:r1]).to(torch.bfloat16)
+    q = (torch.randn(rows, G, 128, generator=gen, device=dev) * scale).contiguous()
+    g = ((q ** 2) * scale ** 2).sum(1).contiguous()
+    st = bp.PlaneStore(K)
+    del K
+    plan = bp.make_plan(g, a.budget)
+    byts = bp.bytes_planes(plan["t"], n)
+    out = torch.empty(rows, G, n, device=dev)
+    for _ in range(3):
+        st.scan(q, plan, out=out)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(a.steps):
+        st.scan(q, plan, out=out)
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / a.steps
+    return {"spec": a.scan_spec, "layers": a.scan_layers, "rows": rows, "launch_ms": ms,
+            "us_per_layer": ms * 1e3 / a.scan_layers, "bytes_per_launch": byts,
+            "achieved_gbs": byts / (ms * 1e-3) / 1e9, "frac_hbm": byts / (ms * 1e-3) / 1e9 / peaks["hbm_gbs"]}
+
+
 def klt_figure(a, bp, off, layers, kvs, n, BH, k_tot, scores):
     """The same decode step over KLT-rotated stores (planesK, scripts/R_ruler.py:63-64, 82-84): per layer
     the query rotation + gains kernel, plan, scan + selection of the rotated queries, attention with the
@@ -914,6 +952,10 @@ def main():
     if a.part == "config3":
         if rank == 0:
             print(json.dumps({"batched_hbm": hbm_figure(a, dev, bp, off, peaks, "config3")}), flush=True)
+        return
+    if a.part == "scan":
+        if rank == 0:
+            print(json.dumps({"scan": scan_part(a, dev, bp, peaks)}), flush=True)
         return
     if a.part == "hf":
         if rank == 0:
