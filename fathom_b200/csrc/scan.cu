@@ -591,13 +591,15 @@ int scan_dispatch(const float* q, int64_t BH, int G, int64_t n, int64_t sub, con
   if (blk_begin == blk_end) return FATHOM_OK;
   const uint32_t* p32 = reinterpret_cast<const uint32_t*>(planes_k);
   if (phase_scan_applies(planes_k, scales_k, sub, nsb, G, n)) {
-    // two phases (16 tokens) per lane for G <= 4 unless that leaves the grid under one wave of warps
+    // two phases (16 tokens) per lane unless that leaves the grid under one wave of warps (G > 6 at
+    // P = 2 spills 96 bytes per thread and still beats P = 1: config 3 batched 55.3 against 60.0 us
+    // per layer)
     const int64_t range = blk_end - blk_begin;
     const bool small = BH * cdiv(range, 8) * 2 < (int64_t)sm_count() * 32;
-    int P = (G <= 4 && !small) ? 2 : 1;
+    int P = small ? 1 : 2;
     if (const char* env = getenv("FATHOM_SCAN_P")) {       // tuning override: 1 or 2 (2 only for G <= 4)
       const int v = atoi(env);
-      if (v == 1 || (v == 2 && G <= 4)) P = v;
+      if (v == 1 || v == 2) P = v;
     }
 #define FATHOM_PH(GG, PP) \
   return launch_phase_scan<GG, PP>(q, BH, n, nblk, nsb, sub, cls, clsn, bmax, p32, scales_k, blk_begin, blk_end, scores, \
@@ -607,10 +609,10 @@ int scan_dispatch(const float* q, int64_t BH, int G, int64_t n, int64_t sub, con
       case 2: if (P == 2) { FATHOM_PH(2, 2) } FATHOM_PH(2, 1)
       case 3: if (P == 2) { FATHOM_PH(3, 2) } FATHOM_PH(3, 1)
       case 4: if (P == 2) { FATHOM_PH(4, 2) } FATHOM_PH(4, 1)
-      case 5: FATHOM_PH(5, 1)
-      case 6: FATHOM_PH(6, 1)
-      case 7: FATHOM_PH(7, 1)
-      case 8: FATHOM_PH(8, 1)
+      case 5: if (P == 2) { FATHOM_PH(5, 2) } FATHOM_PH(5, 1)
+      case 6: if (P == 2) { FATHOM_PH(6, 2) } FATHOM_PH(6, 1)
+      case 7: if (P == 2) { FATHOM_PH(7, 2) } FATHOM_PH(7, 1)
+      case 8: if (P == 2) { FATHOM_PH(8, 2) } FATHOM_PH(8, 1)
     }
 #undef FATHOM_PH
   }
