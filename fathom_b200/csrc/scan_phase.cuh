@@ -22,8 +22,8 @@
 // was 4% and 12% slower on config 1; a zero-weight 8th head for G = 7 was 8% slower than the odd head.)
 //
 // Work split.  A lane owns P phases (P = 2: 16 tokens; P = 1: 8 tokens, for grids under one wave) of
-// one half-word; a warp
-// tile is 4P blocks of one (batch, kv-head) row.  Warps run independently: each streams its tiles'
+// one half-word; a warp tile is 4P blocks of one (batch, kv-head) row.  Warps run independently: each
+// streams its tiles'
 // channel batches through NSTAGE shared-memory stages of its own with 16-byte cp.async copies (a lane
 // per 16 bytes of the tile's (channel, plane) rows and 16-byte scale groups), one commit group per
 // batch, so the main loop has no block-wide barrier.  The epilogue stages each head's scores in the
