@@ -131,11 +131,12 @@ def test_interleaved_kv_rows(where):
     assert torch.equal(a, b)
 
 
-@pytest.mark.parametrize("BH,G", [(2, 4), (40, 4)])
+@pytest.mark.parametrize("BH,G", [(2, 4), (40, 4), (32, 7), (90, 4)])
 def test_in_place_attention_kernels_equal_staged(BH, G):
     """Device-resident rows are read in place (a 4-CTA cluster per query head when the heads are fewer
-    than the SMs, one CTA per head otherwise); host-resident rows go through dedupe + staging.  All
-    three sum in the same order: the outputs are bit-identical, and match the oracle."""
+    than the SMs, one CTA per head otherwise, as for config 3's 224 heads); host-resident rows go
+    through dedupe + staging.  All three sum in the same order: the outputs are bit-identical, and
+    match the oracle."""
     from fathom_b200.offload import MappedBuffer, decode_attention
     cap, k = 3000, 300
     K, V = _kv(BH, cap, BH + G)
