@@ -20,6 +20,8 @@ depends on the previous layer's output in a real model).
           MEASURED_PEAKS.json hbm_gbs (with the Chan4 comparator scans and the KLT-store step)
   chan4_host  the reference's channel-subset comparators (SparQ r = 16, 32 channels) on the same
           host-resident step, for the head-to-head of its offload table
+  copy_index_host  the same step through the reference's copy-index index path (the planes a layer
+          needs staged into device memory in 1, 4 or 8 pipelined chunks, each scanned from HBM)
   hf_decode  end to end through a Qwen3-8B-shaped transformers model (random weights) whose attention
           is patched onto this path, synthetic KV cache in host memory at 256k and 1M tokens: wall and
           CUDA-graph device ms per generated token (`--part hf` adds 512k)
@@ -683,6 +685,38 @@ def chan4_host_figure(a, dev, bp, off, layers, kv, scores):
     return out
 
 
+def copy_index_figure(a, dev, off, layers, kv, scores):
+    """The headline step with the reference's copy-index index path (offload.stream_planes,
+    scripts/B_e2e_offload_v2.py:118-133, 182-196): per layer the planes and scales the plan reads are
+    staged from host into device memory (SM-issued copies) chunk by chunk on a copy stream, and each
+    chunk is scanned from device memory on a scan stream once it has landed; parts = 1 stages the whole
+    layer before one scan.  Same selection (sink_local_topk), row gather and attention as the default
+    zero-copy step, whose figure is the headline; the index bytes moved are the same."""
+    k_tot = a.k + a.sink + a.local
+    byts = float(np.sum([lay.bytes for lay in layers]))
+    out = []
+    for parts in (1, 4, 8):
+        def step():
+            for L, lay in enumerate(layers):
+                rows = kv[L % len(kv)]
+                off.decode_step(lay.q, lay.g, a.budget, lay.store, rows["K"], rows["V"], a.ctx, k_tot, a.sink,
+                                a.local, scores=scores, stream_parts=parts)
+
+        for _ in range(a.warmup):
+            step()
+        torch.cuda.synchronize(dev)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(a.steps):
+            step()
+        e1.record()
+        torch.cuda.synchronize(dev)
+        ms = e0.elapsed_time(e1) / a.steps
+        out.append({"parts": parts, "ms_per_step": ms, "index_bytes_per_step": byts,
+                    "index_gbs_over_step": byts / (ms * 1e-3) / 1e9})
+    return out
+
+
 def chan4_figure(a, bp, layers, peaks, n, BH, scores):
     """The reference's comparator scans on the same keys (kernels/bitplane.py Chan4Store; its kernel table
     rows): SparQ r = 16 (top-16 of sum_g |q_g|), 32 channels, and the full 4-bit scan, each a graph of scans
@@ -1074,6 +1108,10 @@ def main():
             line["config4"] = config4_figure(a, kv_arg, dev, bp, off, rank, world)
             line["config3_replicas"] = config3_replicas(a, dev, bp, off, peaks, rank, world)
     if rank == 0 and world == 1 and not a.no_hbm and a.part == "all":
+        try:
+            line["copy_index_host"] = copy_index_figure(a, dev, off, layers, kv, scores)
+        except Exception as exc:                          # the headline line stands without this figure
+            line["copy_index_host"] = {"error": f"{type(exc).__name__}: {str(exc)[:200]}"}
         try:
             line["chan4_host"] = chan4_host_figure(a, dev, bp, off, layers, kv, scores)
         except Exception as exc:                          # the headline line stands without this figure

@@ -60,6 +60,8 @@ SIGNATURES = {
     "fathom_decode_partial_workspace_bytes": (SZ, [I64, I32, I64]),
     "fathom_decode_attention_partial": (I32, [P, I64, I32, P, I64, P, P, I64, I64, I64, I64, P, P, SZ, P]),
     "fathom_attention_combine": (I32, [P, I64, I64, P, P, P]),
+    "fathom_gather_runs": (I32, [P, P, P, P, P, I64, I64, I64, P]),
+    "fathom_stage_planes": (I32, [P, P, P, I64, I64, I64, I64, P, P, P]),
     "fathom_host_alloc_mapped": (I32, [SZ, ctypes.POINTER(P), ctypes.POINTER(P)]),
     "fathom_host_alloc_mapped_ex": (I32, [SZ, I32, ctypes.POINTER(P), ctypes.POINTER(P)]),
     "fathom_host_free": (I32, [P]),

@@ -591,11 +591,12 @@ int scan_dispatch(const float* q, int64_t BH, int G, int64_t n, int64_t sub, con
   if (blk_begin == blk_end) return FATHOM_OK;
   const uint32_t* p32 = reinterpret_cast<const uint32_t*>(planes_k);
   if (phase_scan_applies(planes_k, scales_k, sub, nsb, G, n)) {
-    // two phases (16 tokens) per lane unless that leaves the grid under one wave of warps (G > 6 at
-    // P = 2 spills 96 bytes per thread and still beats P = 1: config 3 batched 55.3 against 60.0 us
-    // per layer)
+    // two phases (16 tokens) per lane unless one phase per lane still fits the grid in one wave of
+    // resident warps (16 per SM).  Config 1, one layer per launch (8 rows, 2048 warps at P = 2): 14.2
+    // against 17.8 us per layer for P = 1.  G > 6 at P = 2 spills ~100 bytes per thread and still beats
+    // P = 1 (config 3 batched: 53.0 against 59.6 us per layer)
     const int64_t range = blk_end - blk_begin;
-    const bool small = BH * cdiv(range, 8) * 2 < (int64_t)sm_count() * 32;
+    const bool small = BH * cdiv(range, 4) <= (int64_t)sm_count() * 16;
     int P = small ? 1 : 2;
     if (const char* env = getenv("FATHOM_SCAN_P")) {       // tuning override: 1 or 2 (2 only for G <= 4)
       const int v = atoi(env);

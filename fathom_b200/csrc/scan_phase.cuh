@@ -15,11 +15,12 @@
 // float 1 + c_t / 2^t.  Per phase word that is 2t + 2 logic ops plus one prmt per token, against 2t
 // ops per token when f is assembled token by token.
 //
-// Paired FMAs.  The accumulators of two query heads for one token share a 64-bit register pair
-// {acc_g, acc_g+1} and take one fma.rn.f32x2 with {W_g, W_g+1} and f duplicated; an odd last head
-// takes scalar fma.rn.  The halves are independent fma.rn operations, so the sums are those of
-// scan_kernel.  (Measured: pairing two tokens per register with W duplicated, or scalar fma.rn only,
-// was 4% and 12% slower on config 1; a zero-weight 8th head for G = 7 was 8% slower than the odd head.)
+// Paired FMAs.  The accumulators of one query head for two tokens share a 64-bit register pair and
+// take one fma.rn.f32x2 with {f_a, f_b} (each half written by its own byte permute) and the head's
+// weight duplicated {W_g, W_g}, formed once per channel.  The halves are independent fma.rn
+// operations, so the sums are those of scan_kernel.  (Measured against pairing two heads of one token,
+// which copies f into both halves of a pair per token and gives an odd G a scalar head: 8.69 against
+// 9.04 us per layer on config 1 batched, 53.0 against 55.2 on config 3.)
 //
 // Work split.  A lane owns P phases (P = 2: 16 tokens; P = 1: 8 tokens, for grids under one wave) of
 // one half-word; a warp tile is 4P blocks of one (batch, kv-head) row.  Warps run independently: each
@@ -85,28 +86,20 @@ __device__ __forceinline__ uint32_t fbits(uint32_t X, int j) {
 constexpr float F_SCALE = 9223372036854775808.0f;   // 2^63: weights are 2q * 2^63
 constexpr float F_UNSCALE = 9223372036854775808.0f; // sums times 2^63 restore f's scale (2^-126 * 2^63 * 2^63)
 
-// Accumulators of one lane: TPL tokens x G heads.  Pair k2 * TPL + slot holds heads 2k2, 2k2 + 1 of
-// one token (k2 < G / 2); an odd last head has scalar accumulators o[slot].
+// Accumulators of one lane, TPL tokens x G heads: r[g * TPL / 2 + pr] holds head g of the lane's token
+// slots 2pr, 2pr + 1 (see token_of), so one fma.rn.f32x2 takes {f_a, f_b} of two tokens (two byte
+// permutes straight into the register pair) and the head's weight duplicated, {W_g, W_g}.
 template <int G, int P>
 struct Acc {
   static constexpr int TPL = 8 * P;
-  static constexpr int NP = G / 2;                 // full head pairs
-  static constexpr bool ODD = (G & 1) != 0;
-  float2 r[NP > 0 ? NP * TPL : 1];
-  float o[ODD ? TPL : 1];
+  float2 r[G * TPL / 2];
   __device__ __forceinline__ void zero() {
 #pragma unroll
-    for (int i = 0; i < NP * TPL; ++i) r[i] = make_float2(0.f, 0.f);
-    if constexpr (ODD) {
-#pragma unroll
-      for (int i = 0; i < TPL; ++i) o[i] = 0.f;
-    }
+    for (int i = 0; i < G * TPL / 2; ++i) r[i] = make_float2(0.f, 0.f);
   }
-  // value of head g, lane token slot k (k = 2 * pair + half, see token_of)
   __device__ __forceinline__ float get(int g, int k) const {
-    if (ODD && g == G - 1) return o[k];
-    const float2 v = r[(g >> 1) * TPL + k];
-    return (g & 1) ? v.y : v.x;
+    const float2 v = r[g * (TPL / 2) + (k >> 1)];
+    return (k & 1) ? v.y : v.x;
   }
 };
 
@@ -117,19 +110,17 @@ __device__ __forceinline__ int token_of(int k, int r0) {
   else return 4 * (k >> 1) + r0 + (k & 1);                         // phases r0, r0 + 1 of nibble m = k >> 1
 }
 
-// One channel of depth T for one lane: P phase words, then TPL tokens x G heads (G / 2 head pairs
-// with f duplicated, and the odd last head with scalar FMAs).
+// One channel of depth T for one lane: P phase words, then per token pair G paired FMAs
+// {W_g, W_g} x {f_a, f_b}.
 template <int T, int P, int G>
 __device__ __forceinline__ void channel(Acc<G, P>& acc, const uint32_t (&w)[T], const uint32_t (&amt)[P + 3],
-                                        const float2 (&W)[G / 2 > 0 ? G / 2 : 1], float Wo) {
-  constexpr int TPL = 8 * P, NP = G / 2;
+                                        const float2 (&Wd)[G]) {
+  constexpr int TPL = 8 * P;
   uint32_t X[2][2];   // [phase][E, O]
   phase_words<T, 0>(w, amt, X[0][0], X[0][1]);
   if constexpr (P == 2) phase_words<T, 1>(w, amt, X[1][0], X[1][1]);
 #pragma unroll
   for (int pr = 0; pr < TPL / 2; ++pr) {
-    // pair pr: P == 1 -> tokens 8pr + r0 (E byte pr), 8pr + 4 + r0 (O byte pr);
-    //          P == 2 -> nibble m = pr of phases r0, r0 + 1 (E or O byte m >> 1)
     uint32_t xa, xb;
     int j;
     if constexpr (P == 1) {
@@ -141,19 +132,9 @@ __device__ __forceinline__ void channel(Acc<G, P>& acc, const uint32_t (&w)[T], 
       xb = X[1][pr & 1];
       j = pr >> 1;
     }
-    const float fa = __uint_as_float(fbits(xa, j)), fb = __uint_as_float(fbits(xb, j));
-    if constexpr (NP > 0) {
-      const float2 fa2 = make_float2(fa, fa), fb2 = make_float2(fb, fb);
+    const float2 f2 = make_float2(__uint_as_float(fbits(xa, j)), __uint_as_float(fbits(xb, j)));
 #pragma unroll
-      for (int k = 0; k < NP; ++k) {
-        acc.r[k * TPL + 2 * pr] = __ffma2_rn(W[k], fa2, acc.r[k * TPL + 2 * pr]);
-        acc.r[k * TPL + 2 * pr + 1] = __ffma2_rn(W[k], fb2, acc.r[k * TPL + 2 * pr + 1]);
-      }
-    }
-    if constexpr ((G & 1) != 0) {
-      acc.o[2 * pr] = fmaf(Wo, fa, acc.o[2 * pr]);
-      acc.o[2 * pr + 1] = fmaf(Wo, fb, acc.o[2 * pr + 1]);
-    }
+    for (int g = 0; g < G; ++g) acc.r[g * (TPL / 2) + pr] = __ffma2_rn(Wd[g], f2, acc.r[g * (TPL / 2) + pr]);
   }
 }
 
@@ -388,29 +369,28 @@ __global__ void __launch_bounds__(WARPS * 32, (P == 2 && G > 4 ? 3 : 4))
       for (int i = i0; i < i1; ++i) {
         const float s = __half2float(__ushort_as_half(srow16[(i - c0) * (Ge::SROW_U32 * 2) + sidx]));
         const float2 ss = make_float2(s, s);
-        constexpr int NP = G / 2;
-        float2 W[NP > 0 ? NP : 1];
-        float Wo = 0.f;
+        const uint32_t* wr = st + s_slot[i] * Ge::HPW + hw;
+        float2 Wd[G];
 #pragma unroll
         for (int k2 = 0; k2 < G2; ++k2) {
           const float4 v = s_qt[i][k2];
-          if (k2 < NP) W[k2] = __fmul2_rn(make_float2(v.x, v.y), ss);
-          else Wo = v.x * s;                                  // the odd last head (its pair's .y is 0)
+          const float2 wp = __fmul2_rn(make_float2(v.x, v.y), ss);   // {W_2k2, W_2k2+1}
+          Wd[2 * k2] = make_float2(wp.x, wp.x);
+          if (2 * k2 + 1 < G) Wd[2 * k2 + 1] = make_float2(wp.y, wp.y);
           cst[k2] = __ffma2_rn(ss, make_float2(v.z, v.w), cst[k2]);
         }
-        const uint32_t* wr = st + s_slot[i] * Ge::HPW + hw;
         if (c == 0) {
           uint32_t w[1] = {wr[0]};
-          channel<1, P, G>(acc, w, amt, W, Wo);
+          channel<1, P, G>(acc, w, amt, Wd);
         } else if (c == 1) {
           uint32_t w[2] = {wr[0], wr[Ge::HPW]};
-          channel<2, P, G>(acc, w, amt, W, Wo);
+          channel<2, P, G>(acc, w, amt, Wd);
         } else if (c == 2) {
           uint32_t w[3] = {wr[0], wr[Ge::HPW], wr[2 * Ge::HPW]};
-          channel<3, P, G>(acc, w, amt, W, Wo);
+          channel<3, P, G>(acc, w, amt, Wd);
         } else {
           uint32_t w[4] = {wr[0], wr[Ge::HPW], wr[2 * Ge::HPW], wr[3 * Ge::HPW]};
-          channel<4, P, G>(acc, w, amt, W, Wo);
+          channel<4, P, G>(acc, w, amt, Wd);
         }
       }
     }

@@ -172,6 +172,95 @@ def gather_rows(src, cap, idx, BH, dtype=torch.bfloat16, D=128):
     return dst
 
 
+def gather_runs(src, dst, off, ln, nrun, max_len, CH=4096):
+    """Copy run r (int32 words [off[r], off[r] + ln[r])) of src into dst at the same word offsets, for
+    r < nrun[0] (scripts/B_e2e_offload_v2.py:62-71).  off / ln int32 [R] and nrun int32 [1] are device
+    tensors, so the call needs no host sync; zero lengths are skipped.  src / dst: int32 tensors or
+    objects with data_ptr() (a mapped host alias, a DevPtr); every run must lie inside both."""
+    require_cuda(off, ln, nrun)
+    off = off.to(torch.int32).contiguous()
+    ln = ln.to(torch.int32).contiguous()
+    nrun = nrun.to(torch.int32).contiguous()
+    check(lib().fathom_gather_runs(ptr(src), ptr(dst), ptr(off), ptr(ln), ptr(nrun), off.numel(), int(max_len),
+                                   int(CH), stream_of(off.device)), "gather_runs")
+
+
+class PlaneStaging:
+    """Device buffers in the run order of a host store (planes [BH, 1, 128, 4, nblk] int64, scales
+    [BH, 1, 128, nblk] fp16) that receive the staged block ranges of stream_planes.  One staging serves
+    every layer of the same shape; it exposes the attributes PlaneStore.scan reads."""
+
+    def __init__(self, BH, n, device):
+        nblk = math.ceil(n / bp.BLK)
+        self.BH, self.n, self.nblk, self.sub, self.nsb, self.basis = BH, n, nblk, nblk, 1, None
+        self.planes_k = torch.empty(BH, 1, bp.D, 4, nblk, dtype=torch.int64, device=device)
+        self.planes32 = self.planes_k.view(torch.int32)
+        self.scales_k = torch.empty(BH, 1, bp.D, nblk, dtype=torch.float16, device=device)
+
+
+_stagings = {}
+_copy_streams = {}
+
+
+def _staging_for(BH, n, dev):
+    key = (dev, BH, n)
+    s = _stagings.get(key)
+    if s is None:
+        s = _stagings[key] = PlaneStaging(BH, n, dev)
+    return s
+
+
+def _pipeline_streams(dev):
+    s = _copy_streams.get(dev)
+    if s is None:
+        s = _copy_streams[dev] = (torch.cuda.Stream(device=dev), torch.cuda.Stream(device=dev))
+    return s
+
+
+def chunk_bounds(nblk, parts, align=64):
+    """Block ranges [(b0, b1), ...] covering [0, nblk) in `parts` chunks whose inner boundaries are
+    multiples of `align` blocks; empty ranges dropped (scripts/B_e2e_offload_v2.py:106-109)."""
+    parts = max(1, int(parts))
+    bs = [0] + [min(nblk, ((nblk * i // parts) // align) * align) for i in range(1, parts)] + [nblk]
+    return [(a, b) for a, b in zip(bs[:-1], bs[1:]) if b > a]
+
+
+def stream_planes(st, qf, plan, n=None, BH=None, parts=4, staging=None, scores=None):
+    """The chunk-pipelined copy-index scan (stream_planes, scripts/B_e2e_offload_v2.py:118-133) of a
+    host store `st` (HostPlaneStore, run order): for each block chunk, the first t planes of every
+    active channel and its block scales are staged from host memory into device memory on a copy
+    stream (fathom_stage_planes), and the chunk's scan runs from device memory on a scan stream once
+    its copy has landed, so chunk i+1's copy overlaps chunk i's scan.  parts=1 is the unpipelined
+    copy-index mode (:186-196).  The scores are those of st.scan(qf, plan), bit for bit.  staging: a
+    PlaneStaging of the store's shape (one per (device, BH, n) is kept otherwise)."""
+    require_cuda(qf)
+    BH_, G, _ = qf.shape
+    n = st.n if n is None else n
+    BH = BH_ if BH is None else BH
+    if BH != st.BH or n != st.n or st.sub != math.ceil(n / bp.BLK):
+        raise ValueError("stream_planes: the store must hold BH x n tokens in the run order (sub = nblk)")
+    dev = qf.device
+    staging = _staging_for(BH, n, dev) if staging is None else staging
+    scores = torch.empty(BH, G, n, device=dev, dtype=torch.float32) if scores is None else scores
+    t = plan["t"]
+    if t.dtype != torch.int8 or not t.is_contiguous():
+        t = t.to(torch.int8).contiguous()
+    cur = torch.cuda.current_stream(dev)
+    s_copy, s_scan = _pipeline_streams(dev)
+    s_copy.wait_stream(cur)
+    s_scan.wait_stream(cur)
+    for b0, b1 in chunk_bounds(staging.nblk, parts):
+        with torch.cuda.stream(s_copy):
+            check(lib().fathom_stage_planes(ptr(st.planes_k), ptr(st.scales_k), ptr(t), BH, staging.nblk, b0, b1,
+                                            ptr(staging.planes_k), ptr(staging.scales_k), s_copy.cuda_stream),
+                  "stage_planes")
+        s_scan.wait_stream(s_copy)
+        with torch.cuda.stream(s_scan):
+            bp.PlaneStore.scan(staging, qf, plan, out=scores, blocks=(b0, b1))
+    cur.wait_stream(s_scan)
+    return scores
+
+
 def _row_stride(t):
     """Elements between consecutive rows of a K/V source (128 unless it is a strided tensor view)."""
     return t.stride(-2) if isinstance(t, torch.Tensor) and t.dim() >= 2 else 0
@@ -204,10 +293,14 @@ def decode_attention(q, idx, K_src, V_src, cap, n_host=None, K_recent=None, V_re
 
 
 def decode_step(q, g, budget, store, K_src, V_src, cap, k=580, sink=4, local=64, n_host=None, K_recent=None,
-                V_recent=None, recent_cap=0, scores=None, out_dtype=torch.float32):
+                V_recent=None, recent_cap=0, scores=None, out_dtype=torch.float32, stream_parts=0):
     """One layer of an offloaded decode step (offload_attn, scripts/B_e2e_offload_v2.py:180-244, planes
     method): plan -> plane-prefix scan of the (host or HBM) store -> sink+local top-k -> unique-row
     gather + exact attention.  Returns (out [BH,G,128], idx [BH,G,k]).
+
+    stream_parts > 0 (host store only) scans through the copy-index pipeline, stream_planes with that
+    many chunks (the reference's --copy-index --pipeline mode, :182-185), then selects with
+    sink_local_topk; the results are those of the default zero-copy scan, bit for bit.
 
     A store built with a KLT basis (planesK, scripts/R_ruler.py:82-84) is scanned with the rotated
     queries q @ Vt and planned on their gains sum_g (q Vt)^2 * lam (g is then ignored and may be None);
@@ -216,7 +309,11 @@ def decode_step(q, g, budget, store, K_src, V_src, cap, k=580, sink=4, local=64,
     if getattr(store, "basis", None) is not None:
         qs, g = klt_query(q, store.basis)
     plan = bp.make_plan(g, budget)
-    idx = bp.scan_topk(store, qs, plan, k, sink, local, scores=scores)
+    if stream_parts:
+        scores = stream_planes(store, qs, plan, parts=stream_parts, scores=scores)
+        idx = bp.sink_local_topk(scores, k, sink, local)
+    else:
+        idx = bp.scan_topk(store, qs, plan, k, sink, local, scores=scores)
     out = decode_attention(q, idx, K_src, V_src, cap, n_host, K_recent, V_recent, recent_cap, out_dtype)
     return out, idx
 

@@ -284,6 +284,28 @@ int fathom_decode_attention_partial(const float* q, int64_t BH, int G, const int
 int fathom_attention_combine(const float* parts, int64_t P, int64_t rows, float* out_f32, uint16_t* out_bf16,
                              void* stream);
 
+/* ---------------------------------------------------------------- copy-index staging */
+
+/* Copy run r = int32 words [off[r], off[r] + len[r]) of src into dst at the same word offsets, for
+ * r < nrun[0] (a device scalar, so the run count needs no host sync); CTA (r, y) copies words
+ * [y*ch, (y+1)*ch) of its run.  Zero lengths and negative offsets are skipped; every run must lie
+ * inside both buffers.  src and dst need the same alignment modulo 16 bytes; src is normally the
+ * mapped host alias of a host-resident store and dst its device staging (gather_runs_kernel,
+ * scripts/B_e2e_offload_v2.py:62-71).  R runs (grid x), ceil(max_len / ch) <= 65535 chunks. */
+int fathom_gather_runs(const uint32_t* src, uint32_t* dst, const int32_t* off, const int32_t* len,
+                       const int32_t* nrun, int64_t R, int64_t max_len, int64_t ch, void* stream);
+
+/* One chunk of the pipelined copy-index scan (the per-chunk copies of stream_planes,
+ * scripts/B_e2e_offload_v2.py:118-133): for every (bh, channel) with depth t = t[bh][channel] >= 1,
+ * planes 0..t-1 of blocks [b0, b1) and the fp16 scales of those blocks, from a store in the run
+ * order (planes [BH][1][128][4][nblk] uint64, scales [BH][1][128][nblk]; normally mapped host
+ * memory) into a device buffer of the same layout at the same offsets.  Moves bytes_planes(t) of
+ * the block range, nothing for inactive channels.  Sources and staging need the same alignment
+ * modulo 16 bytes. */
+int fathom_stage_planes(const uint64_t* planes_src, const uint16_t* scales_src, const int8_t* t, int64_t BH,
+                        int64_t nblk, int64_t b0, int64_t b1, uint64_t* planes_dst, uint16_t* scales_dst,
+                        void* stream);
+
 /* ---------------------------------------------------------------- host memory */
 
 /* Pinned, portable, mapped host allocation and its device alias (host_mapped,
