@@ -53,6 +53,23 @@ def test_null_and_shape_errors_are_status_codes():
                                       None) == _lib.FATHOM_ERR_SHAPE
     assert L.fathom_klt_query(p, 2, 9, p, p, p, p, None) == _lib.FATHOM_ERR_UNSUPPORTED
     assert L.fathom_klt_query(p, 2, 4, p, None, p, p, None) == _lib.FATHOM_ERR_NULL
+    assert L.fathom_gather_runs(p, None, p, p, p, 4, 100, 64, None) == _lib.FATHOM_ERR_NULL
+    assert L.fathom_gather_runs(p, ctypes.c_void_p(20), p, p, p, 4, 100, 64, None) == _lib.FATHOM_ERR_SHAPE
+    assert L.fathom_gather_runs(p, p, p, p, p, 4, 1 << 30, 1, None) == _lib.FATHOM_ERR_SHAPE   # > 65535 chunks
+    assert L.fathom_stage_planes(p, p, p, 2, 100, 64, 101, p, p, None) == _lib.FATHOM_ERR_SHAPE  # b1 > nblk
+    assert L.fathom_stage_planes(p, p, None, 2, 100, 0, 64, p, p, None) == _lib.FATHOM_ERR_NULL
+
+
+def test_chunk_bounds_cover_the_blocks_with_aligned_inner_edges():
+    from fathom_b200.offload import chunk_bounds
+    assert chunk_bounds(16384, 4) == [(0, 4096), (4096, 8192), (8192, 12288), (12288, 16384)]
+    assert chunk_bounds(1094, 3) == [(0, 320), (320, 704), (704, 1094)]
+    assert chunk_bounds(100, 8) == [(0, 64), (64, 100)]      # empty chunks dropped
+    assert chunk_bounds(79, 1) == [(0, 79)]
+    for nblk, parts in ((5000, 7), (64, 3), (16384, 8)):
+        b = chunk_bounds(nblk, parts)
+        assert b[0][0] == 0 and b[-1][1] == nblk
+        assert all(x[1] == y[0] and x[1] % 64 == 0 for x, y in zip(b, b[1:]))
 
 
 def test_python_layer_rejects_cpu_tensors():
