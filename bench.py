@@ -372,6 +372,9 @@ METRIC = "scanned key-rows/s and decode-step us at 1M ctx, 56-bit, k=512 (1/2/4/
 #     bytes (T = 131072, 8 KV heads, budget 48, 16-byte cp.async instance)
 TRAFFIC_RATIO_HOST = 15359488 / 14151680
 TRAFFIC_RATIO_HBM = 8893952 / 7069127
+# config 3, one layer's scan launch (ncu dram__bytes_read.sum 34.8 MB + dram__bytes_write.sum 61.6 MB, the
+# fp32 scores of 32 rows x 7 heads x 131072 tokens that leave L2, over 28.2 MB of algorithmic index bytes)
+TRAFFIC_RATIO_HBM3 = (34.8 + 61.6) / 28.2
 
 
 def config_dict(a, world):
@@ -484,9 +487,12 @@ def hbm_figure(a, dev, bp, off, peaks, spec="config1", batch=None, seed=None):
             "scan_ms_per_layer": scan_ms, "scan_timing": f"{nl} scan launches in one CUDA graph, mean per launch",
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
                          "frac": achieved / peaks["hbm_gbs"],
-                         "traffic": float(np.mean(byts)) * TRAFFIC_RATIO_HBM if spec == "config1" else None,
+                         "traffic": float(np.mean(byts)) * (TRAFFIC_RATIO_HBM if spec == "config1"
+                                                            else TRAFFIC_RATIO_HBM3),
                          "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum per launch (same shape)"
-                                           if spec == "config1" else "not captured",
+                                           + ("" if spec == "config1" else
+                                              "; writes are the fp32 scores that leave L2 (the selection reads "
+                                              "them back), reads 1.23x the algorithmic bytes"),
                          "bytes_per_launch": float(np.mean(byts))},
             "bits_per_row": float(np.mean(byts)) * 8 / (n * BH),
             "batched_scan": batched,
