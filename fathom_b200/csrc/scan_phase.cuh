@@ -155,17 +155,26 @@ __global__ void __launch_bounds__(WARPS * 32, (P == 2 && G > 4 ? 3 : 4))
   __shared__ uint16_t s_pair[D * NPLANES];
   __shared__ int s_bstart[MAXB + 1], s_wstart[MAXB + 1];
   __shared__ int s_nb, s_cstart[NPLANES + 1];
+  __shared__ float s_q[G][D];                           // the row's queries, staged beside the plan lists
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int bh = blockIdx.y;
-  // ---- the row's channel list in class order, its copy batches and the per-entry head tables
+  // ---- the row's channel list in class order, its copy batches and the per-entry head tables.  The
+  // queries are loaded with the plan lists (thread = channel), not after them, so the set-up waits on
+  // one round of global loads.
+  static_assert(WARPS * 32 == D, "one thread per channel in the set-up");
   int cnt4[NPLANES], ch4[NPLANES];
+  float qrow[G];
+#pragma unroll
+  for (int g = 0; g < G; ++g) qrow[g] = q[(bh * G + g) * D + tid];
 #pragma unroll
   for (int c = 0; c < NPLANES; ++c) {
     const int v = c < bmax ? clsn[bh * bmax + c] : 0;
     cnt4[c] = v < 0 ? 0 : (v > D ? D : v);               // memory safety for foreign plans
     ch4[c] = (c < bmax && tid < D) ? cls[(bh * bmax + c) * D + tid] : 0;
   }
+#pragma unroll
+  for (int g = 0; g < G; ++g) s_q[g][tid] = qrow[g];
   int cstart[NPLANES + 1], cword[NPLANES];
   {
     int st = 0, wd = 0;
@@ -218,7 +227,7 @@ __global__ void __launch_bounds__(WARPS * 32, (P == 2 && G > 4 ? 3 : 4))
       const float KC = __uint_as_float(0x3F800000u - ((uint32_t)t << 23)) - 3.0f;   // 2^-t - 3
       float qv[G];
 #pragma unroll
-      for (int g = 0; g < G; ++g) qv[g] = q[(bh * G + g) * D + ch];
+      for (int g = 0; g < G; ++g) qv[g] = s_q[g][ch];
 #pragma unroll
       for (int k = 0; k < G2; ++k) {
         const float a = 2.0f * qv[2 * k] * F_SCALE, b2 = 2 * k + 1 < G ? 2.0f * qv[2 * k + 1] * F_SCALE : 0.0f;
