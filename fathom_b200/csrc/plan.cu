@@ -13,15 +13,25 @@ namespace {
 
 constexpr int CPL = D / 32;  // channels per lane
 
-__device__ __forceinline__ int warp_exclusive_scan(int v, int lane, int* total) {
-  int x = v;
+// Six exclusive warp prefix sums at once (interleaved shuffles: one scan's latency); tot receives the
+// warp totals.
+__device__ __forceinline__ void warp_exclusive_scan6(int (&v)[6], int lane, int (&tot)[6]) {
+  int x[6];
+#pragma unroll
+  for (int j = 0; j < 6; ++j) x[j] = v[j];
 #pragma unroll
   for (int o = 1; o < 32; o <<= 1) {
-    const int y = __shfl_up_sync(0xffffffffu, x, o);
-    if (lane >= o) x += y;
+#pragma unroll
+    for (int j = 0; j < 6; ++j) {
+      const int y = __shfl_up_sync(0xffffffffu, x[j], o);
+      if (lane >= o) x[j] += y;
+    }
   }
-  *total = __shfl_sync(0xffffffffu, x, 31);
-  return x - v;
+#pragma unroll
+  for (int j = 0; j < 6; ++j) {
+    tot[j] = __shfl_sync(0xffffffffu, x[j], 31);
+    v[j] = x[j] - v[j];
+  }
 }
 
 __global__ void __launch_bounds__(128) plan_kernel(const float* __restrict__ g, const float* __restrict__ budget,
@@ -41,15 +51,45 @@ __global__ void __launch_bounds__(128) plan_kernel(const float* __restrict__ g, 
   }
   const float Br = budget[bh];
   const float bm = (float)bmax;
-  float lo = -60.0f, hi = 60.0f;
-  for (int it = 0; it < iters; ++it) {
-    const float mid = __fmul_rn(__fadd_rn(lo, hi), 0.5f);
-    int cnt = 0;
+  // The depth sum at a candidate mid; a small integer (<= 512): one warp reduction instruction, exact.
+  // rint(x) is formed as (x + 1.5 * 2^23) - 1.5 * 2^23, which rounds half to even like rintf for
+  // |x| < 2^22 (here |x| < 100; NaN and inf pass through as in rintf), and the lane's four clamped
+  // depths are summed as floats: one conversion per evaluation instead of eight, whose pipe bounded
+  // the loop (bisection 2.8 -> 1.8 us).
+  constexpr float RINT_C = 12582912.0f;
+  auto total_at = [&](float mid) {
+    float cnt = 0.0f;
 #pragma unroll
-    for (int i = 0; i < CPL; ++i) cnt += (int)fminf(fmaxf(rintf(__fmul_rn(__fsub_rn(lg[i], mid), 0.5f)), 0.0f), bm);
-    // the depth sum is a small integer (<= 512): one warp reduction instruction, exact
-    const float tot = (float)__reduce_add_sync(0xffffffffu, cnt);
-    if (tot > Br) lo = mid;
+    for (int i = 0; i < CPL; ++i) {
+      const float x = __fmul_rn(__fsub_rn(lg[i], mid), 0.5f);
+      cnt = __fadd_rn(cnt, fminf(fmaxf(__fsub_rn(__fadd_rn(x, RINT_C), RINT_C), 0.0f), bm));
+    }
+    return (float)__reduce_add_sync(0xffffffffu, (int)cnt);
+  };
+  // Bisection, two steps per round: the round's mid and both mids the next step can take (lo, mid)
+  // and (mid, hi) are evaluated together (three independent warp reductions in flight, where one
+  // step's reduction latency bounded the loop), then the path is followed.  Every mid is formed from
+  // the same (lo, hi) as in a one-step loop, so the final hi is bit for bit the same.
+  float lo = -60.0f, hi = 60.0f;
+  int it = 0;
+  for (; it + 2 <= iters; it += 2) {
+    const float m1 = __fmul_rn(__fadd_rn(lo, hi), 0.5f);
+    const float mL = __fmul_rn(__fadd_rn(lo, m1), 0.5f);   // the next mid after hi = m1
+    const float mH = __fmul_rn(__fadd_rn(m1, hi), 0.5f);   // the next mid after lo = m1
+    const float t1 = total_at(m1), tL = total_at(mL), tH = total_at(mH);
+    if (t1 > Br) {
+      lo = m1;
+      if (tH > Br) lo = mH;
+      else hi = mH;
+    } else {
+      hi = m1;
+      if (tL > Br) lo = mL;
+      else hi = mL;
+    }
+  }
+  if (it < iters) {
+    const float mid = __fmul_rn(__fadd_rn(lo, hi), 0.5f);
+    if (total_at(mid) > Br) lo = mid;
     else hi = mid;
   }
   int t[CPL];
@@ -65,9 +105,19 @@ __global__ void __launch_bounds__(128) plan_kernel(const float* __restrict__ g, 
     cnt_pair += t[i];
   }
 
-  int total;
+  // the lane's counts for the six compacted lists (active channels, pairs, the four depth classes),
+  // prefix-summed over the warp together
+  int sc[6] = {cnt_act, cnt_pair, 0, 0, 0, 0};
+#pragma unroll
+  for (int i = 0; i < CPL; ++i) {
+#pragma unroll
+    for (int c = 1; c <= NPLANES; ++c) sc[1 + c] += t[i] == c;
+  }
+  int tot6[6];
+  warp_exclusive_scan6(sc, lane, tot6);
+  int total = tot6[0];
   // active channels, ascending
-  int pos = warp_exclusive_scan(cnt_act, lane, &total);
+  int pos = sc[0];
   int32_t* actb = act + bh * D;
 #pragma unroll
   for (int i = 0; i < CPL; ++i)
@@ -78,22 +128,24 @@ __global__ void __launch_bounds__(128) plan_kernel(const float* __restrict__ g, 
   if (lane == 0) nact[bh] = total;
 
   // (channel, plane) pairs in channel order
-  pos = warp_exclusive_scan(cnt_pair, lane, &total);
+  pos = sc[1];
+  total = tot6[1];
   const int PD = D * bmax;
   int32_t* pb = pairs + bh * PD;
 #pragma unroll
-  for (int i = 0; i < CPL; ++i)
-    for (int p = 0; p < t[i]; ++p) pb[pos++] = (c0 + i) * bmax + p;
+  for (int i = 0; i < CPL; ++i) {
+#pragma unroll
+    for (int p = 0; p < NPLANES; ++p)
+      if (p < t[i]) pb[pos++] = (c0 + i) * bmax + p;
+  }
   for (int e = lane; e < PD; e += 32)
     if (e >= total) pb[e] = 0;
   if (lane == 0) npairs[bh] = total;
 
   // per-depth channel lists
   for (int c = 1; c <= bmax; ++c) {
-    int cnt = 0;
-#pragma unroll
-    for (int i = 0; i < CPL; ++i) cnt += t[i] == c;
-    pos = warp_exclusive_scan(cnt, lane, &total);
+    pos = sc[1 + c];
+    total = tot6[1 + c];
     int32_t* cb = cls + (bh * bmax + (c - 1)) * D;
 #pragma unroll
     for (int i = 0; i < CPL; ++i)
