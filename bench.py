@@ -720,6 +720,7 @@ def copy_index_figure(a, dev, off, layers, kv, scores):
         ms = e0.elapsed_time(e1) / a.steps
         out.append({"parts": parts, "ms_per_step": ms, "index_bytes_per_step": byts,
                     "index_gbs_over_step": byts / (ms * 1e-3) / 1e9})
+    off.release_staging(dev)
     return out
 
 

@@ -210,6 +210,12 @@ def _staging_for(BH, n, dev):
     return s
 
 
+def release_staging(device=None):
+    """Drop the kept PlaneStaging buffers (all devices, or one): ~68 B per token and KV head each."""
+    for key in [k for k in _stagings if device is None or k[0] == torch.device(device)]:
+        del _stagings[key]
+
+
 def _pipeline_streams(dev):
     s = _copy_streams.get(dev)
     if s is None:
@@ -232,7 +238,9 @@ def stream_planes(st, qf, plan, n=None, BH=None, parts=4, staging=None, scores=N
     stream (fathom_stage_planes), and the chunk's scan runs from device memory on a scan stream once
     its copy has landed, so chunk i+1's copy overlaps chunk i's scan.  parts=1 is the unpipelined
     copy-index mode (:186-196).  The scores are those of st.scan(qf, plan), bit for bit.  staging: a
-    PlaneStaging of the store's shape (one per (device, BH, n) is kept otherwise)."""
+    PlaneStaging of the store's shape (otherwise one per (device, BH, n) is kept until
+    release_staging()).  Calls that share a staging must be ordered on the current stream: each call
+    joins its copy and scan streams back into it before returning."""
     require_cuda(qf)
     BH_, G, _ = qf.shape
     n = st.n if n is None else n
