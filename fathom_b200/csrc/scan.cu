@@ -598,7 +598,7 @@ int scan_dispatch(const float* q, int64_t BH, int G, int64_t n, int64_t sub, con
     const int64_t range = blk_end - blk_begin;
     const bool small = BH * cdiv(range, 4) <= (int64_t)sm_count() * 16;
     int P = small ? 1 : 2;
-    if (const char* env = getenv("FATHOM_SCAN_P")) {       // tuning override: 1 or 2 (2 only for G <= 4)
+    if (const char* env = getenv("FATHOM_SCAN_P")) {       // tuning override: 1 or 2
       const int v = atoi(env);
       if (v == 1 || v == 2) P = v;
     }
