@@ -374,15 +374,20 @@ __global__ void __launch_bounds__(WARPS * 32, (P == 2 && G > 4 ? 3 : 4))
     for (int c = 0; c < NPLANES; ++c) {
       const int i0 = c0 > s_cstart[c] ? c0 : s_cstart[c];
       const int i1 = c1 < s_cstart[c + 1] ? c1 : s_cstart[c + 1];
+      if (i0 >= i1) continue;
+      // consecutive channels of one class in one batch: scale rows SROW_U32 words apart, plane words
+      // t = c + 1 rows apart, head tables one entry apart
+      const uint16_t* sp = srow16 + (i0 - c0) * (Ge::SROW_U32 * 2) + sidx;
+      const uint32_t* wr = st + s_slot[i0] * Ge::HPW + hw;
+      const float4* qt = &s_qt[i0][0];
 #pragma unroll 1
-      for (int i = i0; i < i1; ++i) {
-        const float s = __half2float(__ushort_as_half(srow16[(i - c0) * (Ge::SROW_U32 * 2) + sidx]));
+      for (int i = i0; i < i1; ++i, sp += Ge::SROW_U32 * 2, wr += (c + 1) * Ge::HPW, qt += G2) {
+        const float s = __half2float(__ushort_as_half(*sp));
         const float2 ss = make_float2(s, s);
-        const uint32_t* wr = st + s_slot[i] * Ge::HPW + hw;
         float2 Wd[G];
 #pragma unroll
         for (int k2 = 0; k2 < G2; ++k2) {
-          const float4 v = s_qt[i][k2];
+          const float4 v = qt[k2];
           const float2 wp = __fmul2_rn(make_float2(v.x, v.y), ss);   // {W_2k2, W_2k2+1}
           Wd[2 * k2] = make_float2(wp.x, wp.x);
           if (2 * k2 + 1 < G) Wd[2 * k2 + 1] = make_float2(wp.y, wp.y);
