@@ -152,7 +152,7 @@ __global__ void __launch_bounds__(WARPS * 32, (P == 2 && G > 4 ? 3 : 4))
   extern __shared__ __align__(16) uint32_t s_stage[];   // [WARPS][NSTAGE][STAGE_U32]
   __shared__ float4 s_qt[D][G2];                        // flat entry i, g = 2k: {2q_g S, 2q_g+1 S, q_g KC_t, q_g+1 KC_t}
   __shared__ int s_ch[D], s_slot[D];
-  __shared__ uint16_t s_pair[D * NPLANES];
+  __shared__ int s_roff[D * NPLANES];                  // word offset of each (channel, plane) row of a slot
   __shared__ int s_bstart[MAXB + 1], s_wstart[MAXB + 1];
   __shared__ int s_nb, s_cstart[NPLANES + 1];
   __shared__ float s_q[G][D];                           // the row's queries, staged beside the plan lists
@@ -203,7 +203,7 @@ __global__ void __launch_bounds__(WARPS * 32, (P == 2 && G > 4 ? 3 : 4))
       const int slot = cword[c] + t * i;
       const int ch = ch4[c] & (D - 1);
       s_ch[m] = ch;
-      for (int p = 0; p < t; ++p) s_pair[slot + p] = (uint16_t)(ch | (p << 8));
+      for (int p = 0; p < t; ++p) s_roff[slot + p] = (ch * NPLANES + p) * (sub * 2);
       const int b = slot / WB;
       s_slot[m] = slot - b * WB;
       int prev = -1;
@@ -249,7 +249,6 @@ __global__ void __launch_bounds__(WARPS * 32, (P == 2 && G > 4 ? 3 : 4))
 #pragma unroll
   for (int k = 0; k < P + 3; ++k) amt[k] = (uint32_t)(6 - k - r0);
   uint32_t* my_stage = s_stage + (size_t)warp * NSTAGE * Ge::STAGE_U32;
-  const int pstride32 = sub * 2;                          // 32-bit words between (channel, plane) rows
   const uint32_t* planes_row = planes32 + (int64_t)bh * nsb * (D * NPLANES * 2) * sub;
   const uint16_t* scales_row = scales + (int64_t)bh * nsb * D * sub;
   // items = (tile k of this warp, batch b) in order; 32-bit counters, advanced incrementally
@@ -257,11 +256,18 @@ __global__ void __launch_bounds__(WARPS * 32, (P == 2 && G > 4 ? 3 : 4))
 
   auto tile_of = [&](int k) { return tile_lo + gw + k * wstride; };
   // copies of item (k, b) into stage stg: 16-byte chunks, lane e of every 32
+  // the tile's plane and scale rows, formed once per tile (the items of a tile are issued in a row)
+  int rows_k = -1;
+  const uint32_t* rows = planes_row;
+  const uint16_t* srow = scales_row;
   auto issue = [&](int k, int b, int stg) {
-    const int tb0 = tile_of(k) * Ge::BPT;
-    const int sb = tb0 / sub, s_in = tb0 - sb * sub;
-    const uint32_t* rows = planes_row + (sb * (D * NPLANES) * sub + s_in) * 2;
-    const uint16_t* srow = scales_row + sb * D * sub + (s_in & ~7);
+    if (k != rows_k) {
+      const int tb0 = tile_of(k) * Ge::BPT;
+      const int sb = tb0 / sub, s_in = tb0 - sb * sub;
+      rows = planes_row + (sb * (D * NPLANES) * sub + s_in) * 2;
+      srow = scales_row + sb * D * sub + (s_in & ~7);
+      rows_k = k;
+    }
     uint32_t* st = my_stage + stg * Ge::STAGE_U32;
     const int w0 = s_wstart[b], w1 = s_wstart[b + 1], c0 = s_bstart[b], c1 = s_bstart[b + 1];
     const int nrc = (w1 - w0) * Ge::CPR;
@@ -269,9 +275,7 @@ __global__ void __launch_bounds__(WARPS * 32, (P == 2 && G > 4 ? 3 : 4))
     for (int e = lane; e < nch; e += 32) {
       if (e < nrc) {
         const int pos = w0 + e / Ge::CPR, part = e % Ge::CPR;
-        const int pc = s_pair[pos];
-        cp_async16(st + (pos - b * WB) * Ge::HPW + 4 * part,
-                   rows + ((pc & 0xFF) * NPLANES + (pc >> 8)) * pstride32 + 4 * part);
+        cp_async16(st + (pos - b * WB) * Ge::HPW + 4 * part, rows + s_roff[pos] + 4 * part);
       } else {
         const int i = c0 + (e - nrc);
         cp_async16(st + WBUF * Ge::HPW + (i - c0) * Ge::SROW_U32, srow + s_ch[i] * sub);
@@ -307,13 +311,29 @@ __global__ void __launch_bounds__(WARPS * 32, (P == 2 && G > 4 ? 3 : 4))
       const float c = (g & 1) ? cst[g >> 1].y : cst[g >> 1].x;
       uint32_t gm = 0;
       __syncwarp();
+      if constexpr (P == 2 && !GK) {
+        // slots 2m, 2m + 1 are the adjacent tokens 4m + r0, 4m + r0 + 1 (r0 even): one paired FMA and one
+        // 8-byte store per accumulator pair
+        const float2 cc = make_float2(c, c), us = make_float2(F_UNSCALE, F_UNSCALE);
 #pragma unroll
-      for (int k = 0; k < TPL; ++k) {
-        const float v = fmaf(acc.get(g, k), F_UNSCALE, c);   // = (sum of W f) + cst, one rounding
-        const int l = token_of<P>(k, r0);
-        s_sc[hw * Ge::EPI_STRIDE + l] = v;
-        if constexpr (GK) {
-          if (full || (hwt + l >= lo && hwt + l < hi)) gm = max(gm, f2key(v));
+        for (int m = 0; m < TPL / 2; ++m) {
+          const float2 v = __ffma2_rn(acc.r[g * (TPL / 2) + m], us, cc);   // = (sum of W f) + cst, one rounding
+          const int l = 4 * m + r0;
+          *reinterpret_cast<float2*>(s_sc + hw * Ge::EPI_STRIDE + l) = v;
+          if constexpr (GK) {
+            if (full || (hwt + l >= lo && hwt + l < hi)) gm = max(gm, f2key(v.x));
+            if (full || (hwt + l + 1 >= lo && hwt + l + 1 < hi)) gm = max(gm, f2key(v.y));
+          }
+        }
+      } else {
+#pragma unroll
+        for (int k = 0; k < TPL; ++k) {
+          const float v = fmaf(acc.get(g, k), F_UNSCALE, c);   // = (sum of W f) + cst, one rounding
+          const int l = token_of<P>(k, r0);
+          s_sc[hw * Ge::EPI_STRIDE + l] = v;
+          if constexpr (GK) {
+            if (full || (hwt + l >= lo && hwt + l < hi)) gm = max(gm, f2key(v));
+          }
         }
       }
       if constexpr (GK) {
