@@ -249,6 +249,8 @@ def stream_planes(st, qf, plan, n=None, BH=None, parts=4, staging=None, scores=N
         raise ValueError("stream_planes: the store must hold BH x n tokens in the run order (sub = nblk)")
     dev = qf.device
     staging = _staging_for(BH, n, dev) if staging is None else staging
+    if staging.BH != BH or staging.n != n or staging.planes_k.device != dev:
+        raise ValueError(f"stream_planes: the staging must be a PlaneStaging({BH}, {n}) on {dev}")
     scores = torch.empty(BH, G, n, device=dev, dtype=torch.float32) if scores is None else scores
     t = plan["t"]
     if t.dtype != torch.int8 or not t.is_contiguous():
