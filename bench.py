@@ -370,8 +370,8 @@ METRIC = "scanned key-rows/s and decode-step us at 1M ctx, 56-bit, k=512 (1/2/4/
 #     (T = 262144, 8 KV heads, budget 48, bulk-copy instance)
 #   HBM order, phase kernel: dram__bytes_read.sum = 312,030,464 B for 254,251,008 algorithmic bytes (36
 #     layers x 8 KV heads of T = 131072, budget 48, one launch); a single layer's 16.8 MB of scores stay in
-#     L2 between the scan and the selection (dram__bytes_write.sum 0 in the per-layer capture of the
-#     round-1 kernel, same shape), so the per-layer figure counts reads only
+#     L2 between the scan and the selection (dram__bytes_write.sum 0 in a per-layer capture of the
+#     bulk-copy kernel, same shape), so the per-layer figure counts reads only
 TRAFFIC_RATIO_HOST = 15359488 / 14151680
 TRAFFIC_RATIO_HBM = 312030464 / 254251008
 # config 3, one layer's scan launch (ncu dram__bytes_read.sum 34.8 MB + dram__bytes_write.sum 61.6 MB, the
