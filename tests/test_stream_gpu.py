@@ -110,3 +110,43 @@ def test_stream_planes_rejects_a_store_not_in_the_run_order():
     plan = bp.make_plan(d["g"].cuda(), 48.0)
     with pytest.raises(ValueError):
         stream_planes(st, d["q"].cuda(), plan)
+
+
+def test_stream_planes_at_the_bench_context_equals_the_zero_copy_scan():
+    """The headline context (T = 1,048,576, 2 KV heads, G = 4, budget 48), 4 pipelined chunks: bit for bit."""
+    from fathom_b200 import bitplane as bp
+    from fathom_b200.offload import HostPlaneStore, PlaneStaging, stream_planes
+    from fathom_b200.synth import make_layer
+    BH, G, n = 2, 4, 1048576
+    d = make_layer(BH, G, n, seed=5, layer=0, device="cuda", kv_dtype=torch.bfloat16)
+    store = HostPlaneStore(d["K"])
+    del d["K"]
+    plan = bp.make_plan(d["g"], 48.0)
+    direct = store.scan(d["q"], plan)
+    staging = PlaneStaging(BH, n, d["q"].device)
+    streamed = stream_planes(store, d["q"], plan, parts=4, staging=staging)
+    torch.cuda.synchronize()
+    assert torch.equal(streamed, direct)
+    store.free()
+
+
+def test_decode_step_through_the_copy_index_pipeline_with_a_klt_store():
+    """A KLT-rotated host store (planesK): the copy-index path scans the rotated queries like the default."""
+    from fathom_b200 import klt
+    from fathom_b200.offload import HostPlaneStore, MappedBuffer, decode_step
+    from fathom_b200.synth import make_layer
+    BH, G, n, k = 2, 4, 30000, 580
+    d = make_layer(BH, G, n, seed=13, kv_dtype=torch.bfloat16, with_v=True)
+    K, q = d["K"].cuda(), d["q"].cuda()
+    st = HostPlaneStore(K, torch.float32, basis=klt.klt_basis(K))
+    kb, vb = MappedBuffer(K.shape, torch.bfloat16), MappedBuffer(K.shape, torch.bfloat16)
+    kb.host.copy_(d["K"])
+    vb.host.copy_(d["V"])
+    out0, idx0 = decode_step(q, None, 48.0, st, kb.dev, vb.dev, n, k, 4, 64)
+    out1, idx1 = decode_step(q, None, 48.0, st, kb.dev, vb.dev, n, k, 4, 64, stream_parts=3)
+    torch.cuda.synchronize()
+    assert torch.equal(idx1, idx0)
+    assert torch.equal(out1, out0)
+    kb.free()
+    vb.free()
+    st.free()
