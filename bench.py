@@ -374,9 +374,10 @@ METRIC = "scanned key-rows/s and decode-step us at 1M ctx, 56-bit, k=512 (1/2/4/
 #     bulk-copy kernel, same shape), so the per-layer figure counts reads only
 TRAFFIC_RATIO_HOST = 15359488 / 14151680
 TRAFFIC_RATIO_HBM = 312030464 / 254251008
-# config 3, one layer's scan launch (ncu dram__bytes_read.sum 34.8 MB + dram__bytes_write.sum 61.6 MB, the
-# fp32 scores of 32 rows x 7 heads x 131072 tokens that leave L2, over 28.2 MB of algorithmic index bytes)
-TRAFFIC_RATIO_HBM3 = (34.8 + 61.6) / 28.2
+# config 3, one layer's fused scan launch (group keys; scores kept in L2 by an evict-last policy):
+# ncu dram__bytes_read.sum 35,097,856 B + dram__bytes_write.sum 43,120,640 B (the fp32 scores of
+# 32 rows x 7 heads x 131072 tokens that leave L2) over 28,274,688 algorithmic index bytes
+TRAFFIC_RATIO_HBM3 = (35097856 + 43120640) / 28274688
 
 
 def config_dict(a, world):

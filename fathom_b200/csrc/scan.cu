@@ -64,6 +64,28 @@ __device__ __forceinline__ void cp_async16(uint32_t* smem_dst, const void* gsrc)
   const uint32_t d = static_cast<uint32_t>(__cvta_generic_to_shared(smem_dst));
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(d), "l"(gsrc) : "memory");
 }
+// L2 eviction policies (createpolicy) and the accesses that take them: the phase kernel streams its
+// plane words (read once: evict first) and keeps its scores, which the selection reads back (evict last).
+__device__ __forceinline__ uint64_t l2_evict_first() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;\n" : "=l"(p));
+  return p;
+}
+__device__ __forceinline__ uint64_t l2_evict_last() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;\n" : "=l"(p));
+  return p;
+}
+__device__ __forceinline__ void cp_async16_hint(uint32_t* smem_dst, const void* gsrc, uint64_t pol) {
+  const uint32_t d = static_cast<uint32_t>(__cvta_generic_to_shared(smem_dst));
+  asm volatile("cp.async.cg.shared.global.L2::cache_hint [%0], [%1], 16, %2;\n" ::"r"(d), "l"(gsrc), "l"(pol)
+               : "memory");
+}
+__device__ __forceinline__ void st_float4_hint(float* p, const float4& v, uint64_t pol) {
+  asm volatile("st.global.L2::cache_hint.v4.f32 [%0], {%1, %2, %3, %4}, %5;\n" ::"l"(p), "f"(v.x), "f"(v.y),
+               "f"(v.z), "f"(v.w), "l"(pol)
+               : "memory");
+}
 __device__ __forceinline__ void mbar_init(uint64_t* mb) {
   const uint32_t a = static_cast<uint32_t>(__cvta_generic_to_shared(mb));
   asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;\n" ::"r"(a) : "memory");
@@ -532,7 +554,13 @@ int launch_phase_scan(const float* q, int64_t BH, int64_t n, int64_t nblk, int64
   const int64_t tile_lo = b0 / Ge::BPT, tile_hi = cdiv(b1, Ge::BPT);
   const int64_t ntiles = tile_hi - tile_lo;
   const size_t smem = (size_t)ph::WARPS * ph::NSTAGE * Ge::STAGE_U32 * sizeof(uint32_t);
-  auto kernel = gkey ? ph::phase_scan_kernel<G, P, true> : ph::phase_scan_kernel<G, P, false>;
+  // With group keys the selection follows and reads candidate scores back: when the launch's scores
+  // exceed half of L2 they are stored with an evict-last policy and the one-touch plane words loaded
+  // with evict-first (config 3, 117 MB of scores per layer: step 6.44 -> 6.24 ms); smaller score sets
+  // stay in L2 anyway and the plain instance is faster.
+  const bool keep = gkey && (double)BH * G * n * sizeof(float) > 64.0 * 1024 * 1024;
+  auto kernel = gkey ? (keep ? ph::phase_scan_kernel<G, P, true, true> : ph::phase_scan_kernel<G, P, true, false>)
+                     : ph::phase_scan_kernel<G, P, false, false>;
   cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   // tiles per warp: one while the grid fills fewer than ~3 waves of resident CTAs, more (up to 8) to
   // spread each CTA's plan set-up (query and plan tables) over more tiles once it fills many waves

@@ -138,7 +138,7 @@ __device__ __forceinline__ void channel(Acc<G, P>& acc, const uint32_t (&w)[T], 
   }
 }
 
-template <int G, int P, bool GK>
+template <int G, int P, bool GK, bool KEEP>
 __global__ void __launch_bounds__(WARPS * 32, (P == 2 && G > 4 ? 3 : 4))
     phase_scan_kernel(const float* __restrict__ q, const int32_t* __restrict__ cls, const int32_t* __restrict__ clsn,
                       int bmax, const uint32_t* __restrict__ planes32, const uint16_t* __restrict__ scales, int n,
@@ -275,7 +275,10 @@ __global__ void __launch_bounds__(WARPS * 32, (P == 2 && G > 4 ? 3 : 4))
     for (int e = lane; e < nch; e += 32) {
       if (e < nrc) {
         const int pos = w0 + e / Ge::CPR, part = e % Ge::CPR;
-        cp_async16(st + (pos - b * WB) * Ge::HPW + 4 * part, rows + s_roff[pos] + 4 * part);
+        if constexpr (KEEP)   // plane words are read once: evict them first
+          cp_async16_hint(st + (pos - b * WB) * Ge::HPW + 4 * part, rows + s_roff[pos] + 4 * part, l2_evict_first());
+        else
+          cp_async16(st + (pos - b * WB) * Ge::HPW + 4 * part, rows + s_roff[pos] + 4 * part);
       } else {
         const int i = c0 + (e - nrc);
         cp_async16(st + WBUF * Ge::HPW + (i - c0) * Ge::SROW_U32, srow + s_ch[i] * sub);
@@ -348,7 +351,8 @@ __global__ void __launch_bounds__(WARPS * 32, (P == 2 && G > 4 ? 3 : 4))
         const int T = it * 128 + 4 * lane;
         const float4 v = *reinterpret_cast<const float4*>(s_sc + (T >> 5) * Ge::EPI_STRIDE + (T & 31));
         if (vec_ok && (full || (T >= lo && T + 4 <= hi))) {
-          *reinterpret_cast<float4*>(o + T) = v;
+          if constexpr (KEEP) st_float4_hint(o + T, v, l2_evict_last());   // the selection reads them back
+          else *reinterpret_cast<float4*>(o + T) = v;
         } else {
           const float e[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
