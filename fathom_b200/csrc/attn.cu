@@ -3,7 +3,7 @@
 //  HBM twin scripts/B_kernel_bench.py:26-31 gather_attn).
 //
 // decode attention from host-resident rows, three launches (device-resident rows: one launch of
-// attend_direct_kernel or attend_direct_cluster_kernel, which read each pick's rows in place):
+// attend_kernel<.., false>, which reads each pick's rows in place):
 //   1 dedupe   one CTA per (batch, kv-head): the G*k picks go into a shared-memory hash table,
 //              a block scan ranks the distinct indices; slot map (query head, pick) -> unique row,
 //              the unique index list (in table order) and its length.
@@ -11,12 +11,15 @@
 //              (mapped host memory over the host link, or the device-resident recent buffer) into a
 //              device staging area; 16 lanes x 16 B per 256-byte row, 4 rows in flight per lane.
 //              Spreading the rows over every SM keeps enough requests in flight for the link.
-//   3 attend   one CTA of 32 warps per (batch, query head): each warp takes 4 picks at a time from
-//              the staging area (L2-resident), q.K^T / sqrt(128), an online softmax and the running
-//              weighted sum of V; the 16 warp states are merged in shared memory.  fp32 math.
+//   3 attend   16 or 32 warps per (batch, query head), in one CTA or a cluster of 4 or 8 CTAs: a warp
+//              takes 4 picks at a time (8 lanes x 16 dims each) from the staging area (L2-resident),
+//              q.K^T / sqrt(128), an online softmax and the running weighted sum of V; the warp
+//              states are merged in global warp order.  fp32 math.
 // A pick outside the caller's owned index range [idx_lo, idx_hi) is skipped (context shards);
-// the partial form writes the unnormalised output with its (max, sum of exp).
+// the partial form writes the unnormalised output with its (max, sum of exp), base 2.
 #include "common.cuh"
+
+#include <stdlib.h>
 
 #include <cooperative_groups.h>
 
@@ -26,7 +29,6 @@ namespace {
 constexpr int DT = 1024;      // dedupe threads
 constexpr int GT = 256;       // gather threads
 constexpr int GROWS = 64;     // unique rows per gather CTA
-constexpr int AW = 32;        // attend warps
 constexpr int MAX_M = 16384;  // G*k per (batch, kv-head) handled by one dedupe CTA
 
 size_t align256(size_t x) { return (x + 255) & ~(size_t)255; }
@@ -258,294 +260,320 @@ __global__ void __launch_bounds__(GT) gather_kernel(const int32_t* __restrict__ 
   }
 }
 
-__device__ __forceinline__ float bf16lo(uint32_t w) { return __uint_as_float(w << 16); }
-__device__ __forceinline__ float bf16hi(uint32_t w) { return __uint_as_float(w & 0xffff0000u); }
+// ---- attention over the picks --------------------------------------------------------------------
+// Layout shared by every attention kernel (staged host rows, rows read in place, one CTA or a cluster
+// of CTAs per (batch, query head)), so all of them sum in the same order and give the same bits:
+//  * NW warps per (batch, query head) (16, or 32 when the heads are few; fixed by the head count, so
+//    every kernel that serves a launch shape uses the same layout; the CTA split does not change the
+//    sums); global warp w owns picks
+//    [w * PW, w * PW + PW), PW = ceil(k / NW);
+//  * a warp takes PG = 4 picks at once: lane group j (lanes 8j .. 8j + 7) takes picks j, j + 4, j + 8, ..
+//    of each 32-pick chunk, and lane i of a group holds dims [16i, 16i + 16) of q, K, V and the output;
+//  * a score is the group's 8 partial dots summed by 3 shuffles; q is pre-scaled by log2(e) / sqrt(128),
+//    so scores are in base-2 units and weights are exp2(s - m) (the packed partials' m is base 2);
+//  * each group keeps an online softmax (max, sum, 16 dims of the weighted V sum per lane), DU picks
+//    per step; a warp's 4 group states are merged by two symmetric shuffle steps, then the NW warp
+//    states of a (batch, query head) in global warp order.
+constexpr int PG = 4;           // picks per warp instruction (lane groups of 8)
+constexpr int DPL = D / 8;      // dims per lane
+constexpr int DU = 2;           // picks per lane group per step
+constexpr float QSCALE = (float)(1.4426950408889634 / 11.313708498984761);   // log2(e) / sqrt(128)
 
-// The online softmax of one warp over its picks, DU at a time (shared by attend_kernel and the two
-// in-place kernels, so all three sum in the same order and give the same bits).
-struct WarpSoftmax {
-  float m = -INFINITY, l = 0.0f, a0 = 0.0f, a1 = 0.0f, a2 = 0.0f, a3 = 0.0f;
-  __device__ __forceinline__ void add(const float4& qv, const bool (&ok)[8], const uint2 (&kw)[8],
-                                      const uint2 (&vw)[8], float scale) {
-    float sc[8];
+__device__ __forceinline__ float2 bf16x2_f2(uint32_t w) {
+  return make_float2(__uint_as_float(w << 16), __uint_as_float(w & 0xffff0000u));
+}
+
+// One lane's share of its group's online softmax.
+struct GroupSoftmax {
+  float m = -INFINITY, l = 0.0f;
+  float2 a[DPL / 2];
+  __device__ __forceinline__ GroupSoftmax() {
 #pragma unroll
-    for (int u = 0; u < 8; ++u)
-      sc[u] = qv.x * bf16lo(kw[u].x) + qv.y * bf16hi(kw[u].x) + qv.z * bf16lo(kw[u].y) + qv.w * bf16hi(kw[u].y);
+    for (int e = 0; e < DPL / 2; ++e) a[e] = make_float2(0.0f, 0.0f);
+  }
+
+  // DU picks of the group: kr[u] / vr[u] point at this lane's 16 dims of the pick's K and V rows,
+  // nullptr for a pick the group does not own.  sq: this lane's 16 pre-scaled query dims (shared).
+  // Every lane of the warp calls this (the score sums shuffle across the group's lanes).
+  __device__ __forceinline__ void add(const float* sq, const uint16_t* const (&kr)[DU],
+                                      const uint16_t* const (&vr)[DU]) {
+    uint4 kw[DU][2], vw[DU][2];
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
+    for (int u = 0; u < DU; ++u) {
+      if (kr[u] != nullptr) {
+        kw[u][0] = *reinterpret_cast<const uint4*>(kr[u]);
+        kw[u][1] = *reinterpret_cast<const uint4*>(kr[u] + 8);
+        vw[u][0] = *reinterpret_cast<const uint4*>(vr[u]);
+        vw[u][1] = *reinterpret_cast<const uint4*>(vr[u] + 8);
+      } else {
+        kw[u][0] = kw[u][1] = vw[u][0] = vw[u][1] = make_uint4(0, 0, 0, 0);
+      }
+    }
+    float s[DU];
 #pragma unroll
-      for (int u = 0; u < 8; ++u) sc[u] += __shfl_xor_sync(0xffffffffu, sc[u], o);
+    for (int u = 0; u < DU; ++u) {
+      float2 d = make_float2(0.0f, 0.0f);
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const float4 q0 = *reinterpret_cast<const float4*>(sq + 8 * h);
+        const float4 q1 = *reinterpret_cast<const float4*>(sq + 8 * h + 4);
+        d = __ffma2_rn(make_float2(q0.x, q0.y), bf16x2_f2(kw[u][h].x), d);
+        d = __ffma2_rn(make_float2(q0.z, q0.w), bf16x2_f2(kw[u][h].y), d);
+        d = __ffma2_rn(make_float2(q1.x, q1.y), bf16x2_f2(kw[u][h].z), d);
+        d = __ffma2_rn(make_float2(q1.z, q1.w), bf16x2_f2(kw[u][h].w), d);
+      }
+      s[u] = d.x + d.y;
+    }
+#pragma unroll
+    for (int o = 1; o < 8; o <<= 1) {
+#pragma unroll
+      for (int u = 0; u < DU; ++u) s[u] += __shfl_xor_sync(0xffffffffu, s[u], o);
     }
     float mx = m;
 #pragma unroll
-    for (int u = 0; u < 8; ++u) {
-      sc[u] = ok[u] ? sc[u] * scale : -INFINITY;
-      mx = fmaxf(mx, sc[u]);
+    for (int u = 0; u < DU; ++u) {
+      if (kr[u] == nullptr) s[u] = -INFINITY;
+      mx = fmaxf(mx, s[u]);
     }
-    if (mx == -INFINITY) return;  // nothing owned yet
-    const float corr = m == -INFINITY ? 0.0f : expf(m - mx);
-    l *= corr;
-    a0 *= corr;
-    a1 *= corr;
-    a2 *= corr;
-    a3 *= corr;
+    if (mx == -INFINITY) return;   // nothing owned yet
+    if (mx > m) {                  // the running max moved: rescale (a factor of exactly 1 otherwise)
+      const float corr = m == -INFINITY ? 0.0f : exp2f(m - mx);
+      l *= corr;
 #pragma unroll
-    for (int u = 0; u < 8; ++u) {
-      const float pr = sc[u] == -INFINITY ? 0.0f : expf(sc[u] - mx);
-      l += pr;
-      a0 = fmaf(pr, bf16lo(vw[u].x), a0);
-      a1 = fmaf(pr, bf16hi(vw[u].x), a1);
-      a2 = fmaf(pr, bf16lo(vw[u].y), a2);
-      a3 = fmaf(pr, bf16hi(vw[u].y), a3);
+      for (int e = 0; e < DPL / 2; ++e) a[e] = make_float2(a[e].x * corr, a[e].y * corr);
+      m = mx;
     }
-    m = mx;
+#pragma unroll
+    for (int u = 0; u < DU; ++u) {
+      const float p = s[u] == -INFINITY ? 0.0f : exp2f(s[u] - m);
+      l += p;
+      const float2 pp = make_float2(p, p);
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        a[4 * h + 0] = __ffma2_rn(pp, bf16x2_f2(vw[u][h].x), a[4 * h + 0]);
+        a[4 * h + 1] = __ffma2_rn(pp, bf16x2_f2(vw[u][h].y), a[4 * h + 1]);
+        a[4 * h + 2] = __ffma2_rn(pp, bf16x2_f2(vw[u][h].z), a[4 * h + 2]);
+        a[4 * h + 3] = __ffma2_rn(pp, bf16x2_f2(vw[u][h].w), a[4 * h + 3]);
+      }
+    }
+  }
+
+  // Merges the 4 group states of the warp (lanes i, i + 8, i + 16, i + 24 hold the same dims); every
+  // lane ends with the warp's state.  Each step is symmetric in its two states (two rounded products,
+  // then their sum), so all groups hold the same bits.
+  __device__ __forceinline__ void merge_groups() {
+#pragma unroll
+    for (int o = 8; o < 32; o <<= 1) {
+      const float mo = __shfl_xor_sync(0xffffffffu, m, o);
+      const float lo = __shfl_xor_sync(0xffffffffu, l, o);
+      const float M = fmaxf(m, mo);
+      const float e1 = m == -INFINITY ? 0.0f : exp2f(m - M);
+      const float e2 = mo == -INFINITY ? 0.0f : exp2f(mo - M);
+      l = __fadd_rn(__fmul_rn(l, e1), __fmul_rn(lo, e2));
+#pragma unroll
+      for (int e = 0; e < DPL / 2; ++e) {
+        const float ox = __shfl_xor_sync(0xffffffffu, a[e].x, o);
+        const float oy = __shfl_xor_sync(0xffffffffu, a[e].y, o);
+        a[e] = make_float2(__fadd_rn(__fmul_rn(a[e].x, e1), __fmul_rn(ox, e2)),
+                           __fadd_rn(__fmul_rn(a[e].y, e1), __fmul_rn(oy, e2)));
+      }
+      m = M;
+    }
   }
 };
-constexpr int DU = 8;   // rows in flight per warp
 
-// Merges the AW warp states of a CTA and writes the (batch, query head) output or partial.
-__device__ __forceinline__ void attend_finish(const WarpSoftmax& ws, int64_t bhg, float* s_m, float* s_l,
-                                              float (*s_acc)[D], float* __restrict__ out_f32,
-                                              uint16_t* __restrict__ out_bf16, float* __restrict__ out_packed) {
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  if (lane == 0) {
-    s_m[warp] = ws.m;
-    s_l[warp] = ws.l;
-  }
-  s_acc[warp][lane * 4 + 0] = ws.a0;
-  s_acc[warp][lane * 4 + 1] = ws.a1;
-  s_acc[warp][lane * 4 + 2] = ws.a2;
-  s_acc[warp][lane * 4 + 3] = ws.a3;
-  __syncthreads();
-  if (tid < D) {
-    float Mx = -INFINITY;
-#pragma unroll
-    for (int w = 0; w < AW; ++w) Mx = fmaxf(Mx, s_m[w]);
-    float L = 0.0f, O = 0.0f;
-#pragma unroll
-    for (int w = 0; w < AW; ++w) {
-      const float e = s_m[w] == -INFINITY ? 0.0f : expf(s_m[w] - Mx);
-      L = fmaf(s_l[w], e, L);
-      O = fmaf(s_acc[w][tid], e, O);
-    }
-    if (out_packed) {
-      float* pk = out_packed + bhg * (D + 2);
-      pk[tid] = O;
-      if (tid == 0) {
-        pk[D] = Mx;
-        pk[D + 1] = L;
-      }
-    } else {
-      const float o = O / L;
-      if (out_f32) out_f32[bhg * D + tid] = o;
-      if (out_bf16) out_bf16[bhg * D + tid] = __bfloat16_as_ushort(__float2bfloat16_rn(o));
-    }
-  }
-}
+// Where the picks' rows are.  Staged: slot s >= 0 of the staging area (host rows after dedupe + gather).
+// In place: pick t in [idx_lo, idx_hi), row r = t - idx_lo below n_host + recent_cap: row r of the
+// source (r < n_host, row_stride elements apart) or row r - n_host of the recent buffer.
+struct PickRows {
+  const int64_t* idx;       // in place: [BH*G][k] picks
+  const int32_t* slot;      // staged: [BH][M] pick -> staging slot
+  const uint16_t* ksrc;     // staged: kstage [BH][M][128]; in place: the K source
+  const uint16_t* vsrc;
+  int64_t M, cap, row_stride, n_host, recent_cap, idx_lo, idx_hi;
+  const uint16_t* krec;
+  const uint16_t* vrec;
+};
 
-// Host-resident rows, after dedupe + gather: one CTA of AW warps per (batch, query head); warp w owns
-// picks [w*PW, w*PW + PW), PW = ceil(k / AW).  Per 32 picks the warp loads their staging slots with
-// one coalesced load, then reads the staged K and V rows DU picks at a time (8 bytes per lane of each
-// 256-byte row).  out_packed != NULL: partial form, [BH*G][130] = (sum_r e^(s_r - m) V_r, m, l).
-__global__ void __launch_bounds__(AW * 32) attend_kernel(const float* __restrict__ q, int G, int64_t k, int64_t M,
-                                                         const int32_t* __restrict__ slot,
-                                                         const uint16_t* __restrict__ kstage,
-                                                         const uint16_t* __restrict__ vstage,
-                                                         float* __restrict__ out_f32, uint16_t* __restrict__ out_bf16,
-                                                         float* __restrict__ out_packed) {
-  __shared__ float s_m[AW], s_l[AW];
-  __shared__ float s_acc[AW][D];
-  const int64_t bhg = blockIdx.x;
-  const int64_t bh = bhg / G, g = bhg % G;
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const float4 qv = *reinterpret_cast<const float4*>(q + bhg * D + lane * 4);
-  const int32_t* sl = slot + bh * M + g * k;
-  const uint16_t* kb = kstage + bh * M * D + lane * 4;
-  const uint16_t* vb = vstage + bh * M * D + lane * 4;
-  const float scale = rsqrtf((float)D);
-  const int64_t PW = (k + AW - 1) / AW;
-  const int64_t p0 = (int64_t)warp * PW;
-  const int64_t p1 = p0 + PW < k ? p0 + PW : k;
-  WarpSoftmax ws;
-  for (int64_t c0 = p0; c0 < p1; c0 += 32) {   // uniform per warp
-    const int32_t mine = c0 + lane < p1 ? sl[c0 + lane] : -1;
-    const int nc = (int)(p1 - c0 < 32 ? p1 - c0 : 32);
-    for (int s0 = 0; s0 < nc; s0 += DU) {
-      bool ok[DU];
-      uint2 kw[DU], vw[DU];
-#pragma unroll
-      for (int u = 0; u < DU; ++u) {
-        int32_t r = __shfl_sync(0xffffffffu, mine, (s0 + u) & 31);
-        if (s0 + u >= nc) r = -1;
-        ok[u] = r >= 0;
-        kw[u] = ok[u] ? *reinterpret_cast<const uint2*>(kb + (int64_t)r * D) : make_uint2(0, 0);
-        vw[u] = ok[u] ? *reinterpret_cast<const uint2*>(vb + (int64_t)r * D) : make_uint2(0, 0);
-      }
-      ws.add(qv, ok, kw, vw, scale);
-    }
-  }
-  attend_finish(ws, bhg, s_m, s_l, s_acc, out_f32, out_bf16, out_packed);
-}
-
-// Device-resident rows (HBM), many query heads: no dedupe and no staging.  The layout and summation
-// order of attend_kernel, with each pick's K and V rows read in place by index (rows repeated across the
-// query heads of a KV head are L2 hits).  A pick outside [idx_lo, idx_hi) or beyond the readable
-// rows (n_host rows of the source, then recent_cap rows of the recent buffer) is skipped.
-__global__ void __launch_bounds__(AW * 32) attend_direct_kernel(const float* __restrict__ q, int G, int64_t k,
-                                                                const int64_t* __restrict__ idx, int64_t idx_lo,
-                                                                int64_t idx_hi, const uint16_t* __restrict__ ksrc,
-                                                                const uint16_t* __restrict__ vsrc, int64_t cap,
-                                                                int64_t row_stride, int64_t n_host,
-                                                                const uint16_t* __restrict__ krec,
-                                                                const uint16_t* __restrict__ vrec, int64_t recent_cap,
-                                                                float* __restrict__ out_f32,
-                                                                uint16_t* __restrict__ out_bf16,
-                                                                float* __restrict__ out_packed) {
-  __shared__ float s_m[AW], s_l[AW];
-  __shared__ float s_acc[AW][D];
-  const int64_t bhg = blockIdx.x;
-  const int64_t bh = bhg / G;
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const float4 qv = *reinterpret_cast<const float4*>(q + bhg * D + lane * 4);
-  const int64_t* ib = idx + bhg * k;
-  const float scale = rsqrtf((float)D);
-  const int64_t PW = (k + AW - 1) / AW;
-  const int64_t p0 = (int64_t)warp * PW;
-  const int64_t p1 = p0 + PW < k ? p0 + PW : k;
-  WarpSoftmax ws;
-  for (int64_t c0 = p0; c0 < p1; c0 += 32) {   // uniform per warp
-    // this lane's pick of the chunk: its row (< 2^32 - 1, checked by the launcher), or -1 when not owned
-    int32_t rel = -1;
-    if (c0 + lane < p1) {
-      const int64_t t = ib[c0 + lane];
-      if (t >= idx_lo && t < idx_hi && t - idx_lo < n_host + recent_cap) rel = (int32_t)(uint32_t)(t - idx_lo);
-    }
-    const int nc = (int)(p1 - c0 < 32 ? p1 - c0 : 32);
-    for (int s0 = 0; s0 < nc; s0 += DU) {
-      bool ok[DU];
-      uint2 kw[DU], vw[DU];
-#pragma unroll
-      for (int u = 0; u < DU; ++u) {
-        int32_t rr = __shfl_sync(0xffffffffu, rel, (s0 + u) & 31);
-        if (s0 + u >= nc) rr = -1;
-        ok[u] = rr != -1;
-        kw[u] = make_uint2(0, 0);
-        vw[u] = make_uint2(0, 0);
-        if (ok[u]) {
-          const int64_t r = (int64_t)(uint32_t)rr;
-          const uint16_t* kr = r < n_host ? ksrc + (bh * cap + r) * row_stride : krec + (bh * recent_cap + r - n_host) * D;
-          const uint16_t* vr = r < n_host ? vsrc + (bh * cap + r) * row_stride : vrec + (bh * recent_cap + r - n_host) * D;
-          kw[u] = *reinterpret_cast<const uint2*>(kr + lane * 4);
-          vw[u] = *reinterpret_cast<const uint2*>(vr + lane * 4);
-        }
-      }
-      ws.add(qv, ok, kw, vw, scale);
-    }
-  }
-  attend_finish(ws, bhg, s_m, s_l, s_acc, out_f32, out_bf16, out_packed);
-}
-
-// Device-resident rows (HBM), few query heads (fewer than SMs): the pick layout and summation order
-// of attend_kernel, spread over a cluster of CS CTAs of AW / CS warps each: global warp w (CTA w / 8,
-// warp w % 8) owns picks [w*PW, w*PW + PW), PW = ceil(k / AW), and reads each pick's K and V rows in
-// place by index (rows repeated across the query heads of a KV head are L2 hits).  The cluster's
-// first CTA merges the AW warp states through distributed shared memory in global warp order, so the
-// result has the bits of attend_kernel.  A pick outside [idx_lo, idx_hi) or beyond the readable rows
-// (n_host rows of the source, then recent_cap rows of the recent buffer) is skipped.
-constexpr int CS = 4;            // CTAs per (batch, query head)
-constexpr int CW = AW / CS;      // warps per CTA
-__global__ void __launch_bounds__(CW * 32, 1) attend_direct_cluster_kernel(const float* __restrict__ q, int G, int64_t k,
-                                                                const int64_t* __restrict__ idx, int64_t idx_lo,
-                                                                int64_t idx_hi, const uint16_t* __restrict__ ksrc,
-                                                                const uint16_t* __restrict__ vsrc, int64_t cap,
-                                                                int64_t row_stride, int64_t n_host,
-                                                                const uint16_t* __restrict__ krec,
-                                                                const uint16_t* __restrict__ vrec, int64_t recent_cap,
-                                                                float* __restrict__ out_f32,
-                                                                uint16_t* __restrict__ out_bf16,
-                                                                float* __restrict__ out_packed) {
+// NW warps per (batch, query head), CWW per CTA, CS = NW / CWW CTAs (one cluster) per (batch, query
+// head): global warp gw = rank * CWW + warp.  Every warp stores its state into the shared memory of the
+// cluster's first CTA (distributed shared memory; its own when CS = 1), which merges the NW states in
+// global warp order and writes the output or the packed partial [BH*G][130] = (sum_r 2^(s_r - m) V_r,
+// m, l), m in base-2 units.
+template <int NW, int CWW, bool STAGED>
+__global__ void __launch_bounds__(CWW * 32, 32 / CWW) attend_kernel(const float* __restrict__ q, int G, int64_t k,
+                                                                    PickRows pr, float* __restrict__ out_f32,
+                                                                    uint16_t* __restrict__ out_bf16,
+                                                                    float* __restrict__ out_packed) {
   namespace cg = cooperative_groups;
+  constexpr int CS = NW / CWW;
   cg::cluster_group cluster = cg::this_cluster();
-  __shared__ float s_m[CW], s_l[CW];
-  __shared__ float s_acc[CW][D];
-  const unsigned crank = cluster.block_rank();
+  __shared__ __align__(16) float s_q[D];
+  __shared__ float s_m[NW], s_l[NW];               // the cluster's first CTA: every warp's state
+  __shared__ __align__(16) float s_acc[NW][D];
+  const unsigned crank = CS == 1 ? 0u : cluster.block_rank();
   const int64_t bhg = blockIdx.x / CS;
   const int64_t bh = bhg / G;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int gw = (int)crank * CW + warp;   // global warp of the (batch, query head)
-  const float4 qv = *reinterpret_cast<const float4*>(q + bhg * D + lane * 4);
-  const int64_t* ib = idx + bhg * k;
-  const float scale = rsqrtf((float)D);
-  const int64_t PW = (k + AW - 1) / AW;
+  const int grp = lane >> 3, sl = lane & 7;
+  const int gw = (int)crank * CWW + warp;
+  for (int d = tid; d < D; d += CWW * 32) s_q[d] = q[bhg * D + d] * QSCALE;
+  __syncthreads();
+  const float* sq = s_q + sl * DPL;
+  const int64_t PW = (k + NW - 1) / NW;
   const int64_t p0 = (int64_t)gw * PW;
   const int64_t p1 = p0 + PW < k ? p0 + PW : k;
-  WarpSoftmax ws;
+  GroupSoftmax st;
   for (int64_t c0 = p0; c0 < p1; c0 += 32) {   // uniform per warp
-    // this lane's pick of the chunk: its row (< 2^32 - 1, checked by the launcher), or -1 when not owned
-    int32_t rel = -1;
+    // this lane's pick of the chunk: its staging slot or row (< 2^32 - 1, checked by the launcher), -1
+    // when not owned
+    int32_t mine = -1;
     if (c0 + lane < p1) {
-      const int64_t t = ib[c0 + lane];
-      if (t >= idx_lo && t < idx_hi && t - idx_lo < n_host + recent_cap) rel = (int32_t)(uint32_t)(t - idx_lo);
+      if constexpr (STAGED) {
+        mine = pr.slot[bh * pr.M + (bhg % G) * k + c0 + lane];
+      } else {
+        const int64_t t = pr.idx[bhg * k + c0 + lane];
+        if (t >= pr.idx_lo && t < pr.idx_hi && t - pr.idx_lo < pr.n_host + pr.recent_cap)
+          mine = (int32_t)(uint32_t)(t - pr.idx_lo);
+      }
     }
     const int nc = (int)(p1 - c0 < 32 ? p1 - c0 : 32);
-    for (int s0 = 0; s0 < nc; s0 += DU) {
-      bool ok[DU];
-      uint2 kw[DU], vw[DU];
+    for (int s0 = 0; s0 < nc; s0 += PG * DU) {   // uniform per warp
+      const uint16_t* kr[DU];
+      const uint16_t* vr[DU];
 #pragma unroll
       for (int u = 0; u < DU; ++u) {
-        int32_t rr = __shfl_sync(0xffffffffu, rel, (s0 + u) & 31);
-        if (s0 + u >= nc) rr = -1;
-        ok[u] = rr != -1;
-        kw[u] = make_uint2(0, 0);
-        vw[u] = make_uint2(0, 0);
-        if (ok[u]) {
-          const int64_t r = (int64_t)(uint32_t)rr;
-          const uint16_t* kr = r < n_host ? ksrc + (bh * cap + r) * row_stride : krec + (bh * recent_cap + r - n_host) * D;
-          const uint16_t* vr = r < n_host ? vsrc + (bh * cap + r) * row_stride : vrec + (bh * recent_cap + r - n_host) * D;
-          kw[u] = *reinterpret_cast<const uint2*>(kr + lane * 4);
-          vw[u] = *reinterpret_cast<const uint2*>(vr + lane * 4);
+        const int src = s0 + u * PG + grp;
+        int32_t rr = __shfl_sync(0xffffffffu, mine, src & 31);
+        if (src >= nc) rr = -1;
+        kr[u] = vr[u] = nullptr;
+        if (rr != -1) {
+          if constexpr (STAGED) {
+            const int64_t off = (bh * pr.M + rr) * D + sl * DPL;
+            kr[u] = pr.ksrc + off;
+            vr[u] = pr.vsrc + off;
+          } else {
+            const int64_t r = (int64_t)(uint32_t)rr;
+            if (r < pr.n_host) {
+              const int64_t off = (bh * pr.cap + r) * pr.row_stride + sl * DPL;
+              kr[u] = pr.ksrc + off;
+              vr[u] = pr.vsrc + off;
+            } else {
+              const int64_t off = (bh * pr.recent_cap + r - pr.n_host) * D + sl * DPL;
+              kr[u] = pr.krec + off;
+              vr[u] = pr.vrec + off;
+            }
+          }
         }
       }
-      ws.add(qv, ok, kw, vw, scale);
+      st.add(sq, kr, vr);
     }
   }
-  if (lane == 0) {
-    s_m[warp] = ws.m;
-    s_l[warp] = ws.l;
+  st.merge_groups();
+  // each warp stores its state into the first CTA's shared memory (distributed shared memory stores)
+  float* dm = s_m;
+  float* dl = s_l;
+  float* da = &s_acc[0][0];
+  if constexpr (CS > 1) {
+    dm = cluster.map_shared_rank(s_m, 0);
+    dl = cluster.map_shared_rank(s_l, 0);
+    da = cluster.map_shared_rank(&s_acc[0][0], 0);
   }
-  s_acc[warp][lane * 4 + 0] = ws.a0;
-  s_acc[warp][lane * 4 + 1] = ws.a1;
-  s_acc[warp][lane * 4 + 2] = ws.a2;
-  s_acc[warp][lane * 4 + 3] = ws.a3;
-  cluster.sync();   // every CTA's warp states are written
-  if (crank == 0 && tid < D) {
+  if (lane == 0) {
+    dm[gw] = st.m;
+    dl[gw] = st.l;
+  }
+  if (lane < 8) {
+    float4* dst = reinterpret_cast<float4*>(da + gw * D + sl * DPL);
+#pragma unroll
+    for (int e = 0; e < DPL / 4; ++e)
+      dst[e] = make_float4(st.a[2 * e].x, st.a[2 * e].y, st.a[2 * e + 1].x, st.a[2 * e + 1].y);
+  }
+  if constexpr (CS == 1) __syncthreads();
+  else cluster.sync();   // every warp's state is in the first CTA's shared memory
+  if (crank != 0) return;
+  for (int d = tid; d < D; d += CWW * 32) {
     float Mx = -INFINITY;
-    for (int w = 0; w < AW; ++w) Mx = fmaxf(Mx, *cluster.map_shared_rank(&s_m[w % CW], w / CW));
+#pragma unroll 8
+    for (int w = 0; w < NW; ++w) Mx = fmaxf(Mx, s_m[w]);
     float L = 0.0f, O = 0.0f;
-    for (int w = 0; w < AW; ++w) {
-      const float mw = *cluster.map_shared_rank(&s_m[w % CW], w / CW);
-      const float e = mw == -INFINITY ? 0.0f : expf(mw - Mx);
-      L = fmaf(*cluster.map_shared_rank(&s_l[w % CW], w / CW), e, L);
-      O = fmaf(*cluster.map_shared_rank(&s_acc[w % CW][tid], w / CW), e, O);
+#pragma unroll 8
+    for (int w = 0; w < NW; ++w) {
+      const float e = s_m[w] == -INFINITY ? 0.0f : exp2f(s_m[w] - Mx);
+      L = fmaf(s_l[w], e, L);
+      O = fmaf(s_acc[w][d], e, O);
     }
     if (out_packed) {
       float* pk = out_packed + bhg * (D + 2);
-      pk[tid] = O;
-      if (tid == 0) {
+      pk[d] = O;
+      if (d == 0) {
         pk[D] = Mx;
         pk[D + 1] = L;
       }
     } else {
       const float o = O / L;
-      if (out_f32) out_f32[bhg * D + tid] = o;
-      if (out_bf16) out_bf16[bhg * D + tid] = __bfloat16_as_ushort(__float2bfloat16_rn(o));
+      if (out_f32) out_f32[bhg * D + d] = o;
+      if (out_bf16) out_bf16[bhg * D + d] = __bfloat16_as_ushort(__float2bfloat16_rn(o));
     }
   }
-  cluster.sync();   // the first CTA has read the others' shared memory
 }
 
-// out = sum_p o_p e^(m_p - M) / sum_p l_p e^(m_p - M), M = max_p m_p: log-sum-exp merge of the
-// partial attention of P context shards.  One CTA of 128 threads per (batch, query head).
+// Warps and CTAs per (batch, query head) for `rows` of them: 32 warps in a cluster of 8 CTAs for fewer
+// than SMs / 4 heads (latency: short per-group pick chains), 16 warps in a cluster of 4 up to 2 x SMs
+// heads, one CTA of 16 warps beyond (measured on config-1, config-3 and 360-head launches).
+// FATHOM_ATTN_NW (16 or 32) and FATHOM_ATTN_CS (1, 2, 4 or 8) override (tuning).
+void attend_shape(int64_t rows, int* nw, int* cs) {
+  const int64_t sms = sm_count();
+  *nw = rows * 4 >= sms ? 16 : 32;
+  *cs = rows >= 2 * sms ? 1 : rows * 4 >= sms ? 4 : 8;
+  if (const char* e = getenv("FATHOM_ATTN_NW")) *nw = atoi(e) == 32 ? 32 : 16;
+  if (const char* e = getenv("FATHOM_ATTN_CS")) {
+    const int v = atoi(e);
+    *cs = (v == 1 || v == 2 || v == 4 || v == 8) ? v : *cs;
+  }
+}
+
+template <int NW, bool STAGED>
+cudaError_t launch_attend_nw(cudaLaunchConfig_t* cfg, int cs, const float* q, int G, int64_t k, const PickRows& pr,
+                             float* out_f32, uint16_t* out_bf16, float* out_packed) {
+  cfg->blockDim = dim3((unsigned)(NW / cs * 32));
+  switch (cs) {
+    case 1: return cudaLaunchKernelEx(cfg, attend_kernel<NW, NW, STAGED>, q, G, k, pr, out_f32, out_bf16, out_packed);
+    case 2:
+      return cudaLaunchKernelEx(cfg, attend_kernel<NW, NW / 2, STAGED>, q, G, k, pr, out_f32, out_bf16, out_packed);
+    case 4:
+      return cudaLaunchKernelEx(cfg, attend_kernel<NW, NW / 4, STAGED>, q, G, k, pr, out_f32, out_bf16, out_packed);
+    default:
+      return cudaLaunchKernelEx(cfg, attend_kernel<NW, NW / 8, STAGED>, q, G, k, pr, out_f32, out_bf16, out_packed);
+  }
+}
+
+template <bool STAGED>
+int launch_attend(const float* q, int64_t BH, int G, int64_t k, const PickRows& pr, float* out_f32,
+                  uint16_t* out_bf16, float* out_packed, cudaStream_t st) {
+  const int64_t rows = BH * G;
+  int nw = 16, cs = 1;
+  attend_shape(rows, &nw, &cs);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)(rows * cs));
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = (unsigned)cs;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = cs > 1 ? 1 : 0;
+  const cudaError_t e = nw == 32 ? launch_attend_nw<32, STAGED>(&cfg, cs, q, G, k, pr, out_f32, out_bf16, out_packed)
+                                 : launch_attend_nw<16, STAGED>(&cfg, cs, q, G, k, pr, out_f32, out_bf16, out_packed);
+  if (e != cudaSuccess) return set_error(FATHOM_ERR_CUDA, "decode_attention: launch: %s", cudaGetErrorString(e));
+  return check_launch("decode_attention");
+}
+
+// out = sum_p o_p 2^(m_p - M) / sum_p l_p 2^(m_p - M), M = max_p m_p: log-sum-exp merge of the
+// partial attention of P context shards (m in base-2 units).  One CTA of 128 threads per (batch,
+// query head).
 __global__ void __launch_bounds__(D) combine_kernel(const float* __restrict__ parts, int64_t P, int64_t rows,
                                                     float* __restrict__ out_f32, uint16_t* __restrict__ out_bf16) {
   const int64_t row = blockIdx.x;
@@ -557,7 +585,7 @@ __global__ void __launch_bounds__(D) combine_kernel(const float* __restrict__ pa
   for (int64_t p = 0; p < P; ++p) {
     const float* pp = parts + (p * rows + row) * W;
     const float m = pp[D];
-    const float w = m == -INFINITY ? 0.0f : expf(m - M);
+    const float w = m == -INFINITY ? 0.0f : exp2f(m - M);
     L = fmaf(pp[D + 1], w, L);
     acc = fmaf(pp[t], w, acc);
   }
@@ -606,29 +634,12 @@ int run_decode(const float* q, int64_t BH, int G, const int64_t* idx, int64_t k,
   if (device_memory(K_src) && device_memory(V_src) &&
       (recent_cap == 0 || (device_memory(K_recent) && device_memory(V_recent)))) {
     // rows already in HBM: each pick's rows are read in place (one launch; the workspace is unused)
-    if (BH * G >= (int64_t)sm_count()) {   // enough CTAs of 32 warps to fill the GPU
-      attend_direct_kernel<<<(unsigned)(BH * G), AW * 32, 0, st>>>(q, G, k, idx, idx_lo, idx_hi, K_src, V_src, cap,
-                                                                   kv_row_stride, n_host, K_recent, V_recent,
-                                                                   recent_cap, out_f32, out_bf16, out_packed);
-      return check_launch("decode_attention");
-    }
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3((unsigned)(BH * G * CS));
-    cfg.blockDim = dim3(CW * 32);
-    cfg.dynamicSmemBytes = 0;
-    cfg.stream = st;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = CS;
-    attr[0].val.clusterDim.y = 1;
-    attr[0].val.clusterDim.z = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    const cudaError_t e = cudaLaunchKernelEx(&cfg, attend_direct_cluster_kernel, q, G, k, idx, idx_lo, idx_hi, K_src, V_src,
-                                             cap, kv_row_stride, n_host, K_recent, V_recent, recent_cap, out_f32,
-                                             out_bf16, out_packed);
-    if (e != cudaSuccess) return set_error(FATHOM_ERR_CUDA, "decode_attention: launch: %s", cudaGetErrorString(e));
-    return check_launch("decode_attention");
+    FATHOM_REQUIRE(recent_cap == 0 || ((reinterpret_cast<uintptr_t>(K_recent) & 15) == 0 &&
+                                       (reinterpret_cast<uintptr_t>(V_recent) & 15) == 0),
+                   FATHOM_ERR_SHAPE, "decode_attention: the recent buffers must be 16-byte aligned");
+    const PickRows pr{idx, nullptr, K_src, V_src, 0, cap, kv_row_stride, n_host, recent_cap, idx_lo, idx_hi,
+                      K_recent, V_recent};
+    return launch_attend<false>(q, BH, G, k, pr, out_f32, out_bf16, out_packed, st);
   }
   DecodeWs w = carve(workspace, BH, M);
   int log2ts = 10;
@@ -647,9 +658,10 @@ int run_decode(const float* q, int64_t BH, int G, const int64_t* idx, int64_t k,
                                       reinterpret_cast<const uint4*>(K_recent),
                                       reinterpret_cast<const uint4*>(V_recent), recent_cap,
                                       reinterpret_cast<uint4*>(w.kstage), reinterpret_cast<uint4*>(w.vstage));
-  attend_kernel<<<(unsigned)(BH * G), AW * 32, 0, st>>>(q, G, k, M, w.slot, w.kstage, w.vstage, out_f32, out_bf16,
-                                                         out_packed);
-  return check_launch("decode_attention");
+  const int r = check_launch("decode_attention (dedupe, gather)");
+  if (r != FATHOM_OK) return r;
+  const PickRows pr{nullptr, w.slot, w.kstage, w.vstage, M, 0, 0, 0, 0, 0, 0, nullptr, nullptr};
+  return launch_attend<true>(q, BH, G, k, pr, out_f32, out_bf16, out_packed, st);
 }
 
 }  // namespace

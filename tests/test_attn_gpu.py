@@ -133,9 +133,9 @@ def test_interleaved_kv_rows(where):
 
 @pytest.mark.parametrize("BH,G", [(2, 4), (40, 4), (32, 7), (90, 4)])
 def test_in_place_attention_kernels_equal_staged(BH, G):
-    """Device-resident rows are read in place (a 4-CTA cluster per query head when the heads are fewer
-    than the SMs, one CTA per head otherwise, as for config 3's 224 heads); host-resident rows go
-    through dedupe + staging.  All three sum in the same order: the outputs are bit-identical, and
+    """Device-resident rows are read in place (8 heads: 32 warps per head in 8-CTA clusters; 160 and
+    config 3's 224 heads: 16 warps in 4-CTA clusters; 360: one 16-warp CTA per head); host-resident
+    rows go through dedupe + staging.  Both sum in the same order: the outputs are bit-identical, and
     match the oracle."""
     from fathom_b200.offload import MappedBuffer, decode_attention
     cap, k = 3000, 300
@@ -153,5 +153,32 @@ def test_in_place_attention_kernels_equal_staged(BH, G):
                              O.bf16_to_f32(V.view(torch.int16).numpy().view(np.uint16)), idx.numpy())
     out = dev_out.cpu().numpy()
     assert np.abs(out - ref).max() <= 1e-5 * np.abs(ref).max() + 1e-6
+    kb.free()
+    vb.free()
+
+
+@pytest.mark.parametrize("nw", [16, 32])
+def test_attention_bits_do_not_depend_on_the_cta_split(nw, monkeypatch):
+    """The warps of a query head may sit in one CTA or in a cluster of 2, 4 or 8 CTAs (the tuning
+    overrides pick the split); the merge runs in global warp order, so every split gives the same bits,
+    from device rows and from staged host rows."""
+    from fathom_b200.offload import MappedBuffer, decode_attention
+    BH, G, k, cap = 3, 5, 1000, 20000
+    K, V = _kv(BH, cap, 123)
+    g = torch.Generator().manual_seed(9)
+    q = torch.randn(BH, G, 128, generator=g).cuda()
+    idx = torch.randint(0, cap, (BH, G, k), generator=g).cuda()
+    kb, vb = MappedBuffer(K.shape, torch.bfloat16), MappedBuffer(V.shape, torch.bfloat16)
+    kb.host.copy_(K)
+    vb.host.copy_(V)
+    monkeypatch.setenv("FATHOM_ATTN_NW", str(nw))
+    outs = []
+    for cs in (1, 2, 4, 8):
+        monkeypatch.setenv("FATHOM_ATTN_CS", str(cs))
+        outs.append(decode_attention(q, idx, K.cuda(), V.cuda(), cap))
+        outs.append(decode_attention(q, idx, kb.dev, vb.dev, cap))
+    torch.cuda.synchronize()
+    for o in outs[1:]:
+        assert torch.equal(o, outs[0])
     kb.free()
     vb.free()
