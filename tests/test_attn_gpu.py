@@ -182,3 +182,39 @@ def test_attention_bits_do_not_depend_on_the_cta_split(nw, monkeypatch):
         assert torch.equal(o, outs[0])
     kb.free()
     vb.free()
+
+
+@pytest.mark.parametrize("where", ["device", "host"])
+def test_attention_skips_picks_outside_the_readable_rows(where):
+    """Picks that are negative or at or past the readable rows (n_host source rows + recent_cap recent
+    rows) are skipped: the output is the attention over the remaining picks, in place and staged."""
+    from fathom_b200.offload import MappedBuffer, decode_attention
+    BH, G, k, cap, n_host, rc = 3, 4, 300, 6000, 5900, 50
+    K, V = _kv(BH, cap, 31)
+    Kr, Vr = _kv(BH, rc, 32)
+    g = torch.Generator().manual_seed(33)
+    q = torch.randn(BH, G, 128, generator=g)
+    idx = torch.randint(0, n_host + rc, (BH, G, k), generator=g)
+    bad = torch.rand(BH, G, k, generator=g) < 0.2
+    junk = torch.where(torch.rand(BH, G, k, generator=g) < 0.5, torch.full_like(idx, -1),
+                       torch.randint(n_host + rc, 1 << 30, (BH, G, k), generator=g))
+    idx = torch.where(bad, junk, idx)
+    if where == "device":
+        Ks, Vs = K.cuda(), V.cuda()
+    else:
+        kb, vb = MappedBuffer(K.shape, torch.bfloat16), MappedBuffer(V.shape, torch.bfloat16)
+        kb.host.copy_(K)
+        vb.host.copy_(V)
+        Ks, Vs = kb.dev, vb.dev
+    out = decode_attention(q.cuda(), idx.cuda(), Ks, Vs, cap, n_host, Kr.cuda(), Vr.cuda(), rc).cpu().numpy()
+    f = lambda t: O.bf16_to_f32(t.view(torch.int16).numpy().view(np.uint16))
+    ref = np.empty_like(out)
+    for b in range(BH):
+        for h in range(G):
+            ok = idx[b, h][~bad[b, h]].numpy()[None, None, :]
+            ref[b, h] = O.decode_attention(q[b:b + 1, h:h + 1].numpy(), f(K[b:b + 1]), f(V[b:b + 1]), ok,
+                                           f(Kr[b:b + 1]), f(Vr[b:b + 1]), n_host)[0, 0]
+    assert np.abs(out - ref).max() <= 1e-5 * np.abs(ref).max() + 1e-6
+    if where == "host":
+        kb.free()
+        vb.free()
